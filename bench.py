@@ -1,0 +1,407 @@
+#!/usr/bin/env python
+"""Throughput of the batched Jonker-Volgenant op (problems solved per second).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c2] [--impl ours|reference]
+
+One step = one call of torch.ops.assignment.jonker_dense_batch on a resident
+(B, N, M) fp32 batch (statistics pass, host check of the NaN / -inf verdict,
+solve).  At N > 1 (torchrun, one rank per GPU) every rank holds a contiguous
+slice of one global batch and runs torchmatch_b200.sharded.solve_sharded (one
+all-reduce of the statistics words, then a local solve): the per-rank work is
+fixed, so scaling is weak.  Rank 0 prints one JSON line.
+
+Workloads (synthetic, seeded; tests/golden/cases.py holds the recipes):
+  c1  B=64     N=M=32   uniform[0,1)                (configs[0], CPU case)
+  c2  B=4096   N=M=64   uniform[0,1)                (configs[1], default)
+  c3  B=16384  N=M=128  integers in {0..15}
+  c4  B=8192   N=100 M=150 uniform[0,10), 20% +inf
+  c5  B=65536  N=M=256  |x_i - y_j|^2, x, y ~ N(0, I16)  (B split over ranks)
+
+`value` is device time (CUDA events, max over ranks) with inputs resident in
+HBM; consecutive steps rotate over enough input copies that their total
+exceeds twice the 126 MB L2, so every step reads its batch from HBM.  `e2e`
+is the same op with a pinned host batch copied in and the result copied out
+inside each timed step.  `roofline` is measured live: the solve kernel alone,
+launched through the C ABI between CUDA events on its stream, against the
+measured HBM copy bandwidth.  `cpu_baseline` times the reference's own CPU
+solver (oracle/_ref, built from the reference sources) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests" / "golden"))
+
+METRIC = ("LAPs solved/sec (B×N×M fp32 batch) at 1/2/4/8 B200; "
+          "% of HBM roofline")
+UNIT = "problems/s"
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+CONFIGS = {
+    "c1": dict(B=64, N=32, M=32, desc="config1: B=64 N=M=32 uniform[0,1) fp32"),
+    "c2": dict(B=4096, N=64, M=64, desc="config2: B=4096 N=M=64 uniform[0,1) fp32"),
+    "c3": dict(B=16384, N=128, M=128, desc="config3: B=16384 N=M=128 integers {0..15} fp32"),
+    "c4": dict(B=8192, N=100, M=150, desc="config4: B=8192 N=100 M=150 uniform[0,10) 20% +inf"),
+    "c5": dict(B=65536, N=256, M=256, desc="config5: B=65536 N=M=256 |x-y|^2, x,y~N(0,I16)",
+               split=True),
+}
+
+
+def make_batch(cfg: str, b: int, seed: int):
+    """Seeded CPU batch of workload `cfg` with b problems."""
+    import torch
+
+    import cases
+
+    if cfg == "c1":
+        return cases.config1()[:b]
+    if cfg == "c2":
+        return torch.rand(b, 64, 64, generator=torch.Generator().manual_seed(seed))
+    if cfg == "c3":
+        return torch.randint(0, 16, (b, 128, 128),
+                             generator=torch.Generator().manual_seed(seed)).float()
+    if cfg == "c4":
+        g = torch.Generator().manual_seed(seed)
+        c = torch.rand(b, 100, 150, generator=g) * 10
+        mask = torch.rand(b, 100, 150, generator=g) < 0.2
+        i = torch.arange(100)
+        mask[:, i, i] = False
+        return c.masked_fill(mask, float("inf"))
+    if cfg == "c5":
+        return cases.config5_chunk(b, seed)
+    raise ValueError(cfg)
+
+
+def make_batch_device(cfg: str, b: int, seed: int, device):
+    """Same distribution generated on the GPU (timing only; parity runs use
+    the CPU recipes)."""
+    import torch
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    if cfg == "c5":
+        out = torch.empty(b, 256, 256, device=device)
+        for s in range(0, b, 512):
+            e = min(b, s + 512)
+            x = torch.randn(e - s, 256, 16, device=device, generator=g)
+            y = torch.randn(e - s, 256, 16, device=device, generator=g)
+            out[s:e] = ((x[:, :, None] - y[:, None]) ** 2).sum(-1)
+        return out
+    if cfg == "c3":
+        return torch.randint(0, 16, (b, 128, 128), device=device, generator=g).float()
+    if cfg == "c4":
+        c = torch.rand(b, 100, 150, device=device, generator=g) * 10
+        mask = torch.rand(b, 100, 150, device=device, generator=g) < 0.2
+        i = torch.arange(100, device=device)
+        mask[:, i, i] = False
+        return c.masked_fill(mask, float("inf"))
+    return make_batch(cfg, b, seed).to(device)
+
+
+def peak_hbm():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        v = float(json.loads(p.read_text())["hbm_gbs"])
+        return v, "MEASURED_PEAKS.json hbm_gbs (of measured)"
+    except Exception:
+        return FALLBACK_HBM_GBS, "profiling-recipe fallback 6.65 TB/s (of fallback)"
+
+
+def traffic_for(cfg: str):
+    """DRAM bytes per solve launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    try:
+        return json.loads(p.read_text()).get(cfg)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.gpu)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in self.rows for k in range(4) if r[5 + k] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def cpu_baseline(cfg: str, seconds: float = 6.0):
+    """The reference's CPU solver (oracle/_ref) -- else the oracle port -- on
+    all host threads over a bounded sample of the workload."""
+    import oracle
+
+    kind = "reference" if oracle.reference_available() else "port"
+    fn = oracle.reference_jonker_dense_batch if kind == "reference" else oracle.jonker_dense_batch
+    spec = CONFIGS[cfg]
+    b = min(spec["B"], {"c3": 2048, "c4": 2048, "c5": 512}.get(cfg, spec["B"]))
+    x = make_batch(cfg, b, 0).numpy()
+    threads = oracle.host_threads()
+    fn(x[: min(b, 64)], threads)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 50):
+        t0 = time.perf_counter()
+        fn(x, threads)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": b / med, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{spec['desc'].split(':')[0]} first {b} problems x {len(times)} runs, "
+                      f"median {med * 1e3:.1f} ms, {threads} threads"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+
+    kind = "reference" if oracle.reference_available() else "port"
+    fn = oracle.reference_jonker_dense_batch if kind == "reference" else oracle.jonker_dense_batch
+    spec = CONFIGS[args.config]
+    b = min(spec["B"], {"c3": 2048, "c4": 2048, "c5": 512}.get(args.config, spec["B"]))
+    x = make_batch(args.config, b, 0).numpy()
+    threads = oracle.host_threads()
+    for _ in range(args.warmup):
+        fn(x, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn(x, threads)
+    dt = time.perf_counter() - t0
+    value = b * args.steps / dt
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": spec["desc"], "sample_problems": b},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"first {b} problems of the workload per step"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    import torchmatch_b200  # noqa: F401
+    from torchmatch_b200 import _loader, sharded
+
+    lib = _loader.core()
+    spec = CONFIGS[args.config]
+    n, m = spec["N"], spec["M"]
+    b = spec["B"] // world if spec.get("split") else spec["B"]
+    per_bytes = b * n * m * 4
+    nbuf = max(1, min(8, -(-2 * L2_BYTES // per_bytes) + 1)) if per_bytes < 2 * L2_BYTES else 1
+    bufs = [make_batch_device(args.config, b, 1000 * rank + k, dev) for k in range(nbuf)]
+    op = torch.ops.assignment.jonker_dense_batch
+
+    def step(x):
+        if world > 1:
+            return sharded.solve_sharded(x)
+        return op(x)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    gpu_index = local
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        try:
+            gpu_index = int(vis.split(",")[local])
+        except ValueError:
+            pass
+    clocks = ClockSampler(gpu_index) if rank == 0 else None
+
+    for k in range(args.warmup):
+        step(bufs[k % nbuf])
+    barrier()
+    if clocks:
+        clocks.start()
+        t_load = time.perf_counter() + 0.5
+        while time.perf_counter() < t_load:  # let the sampler see the GPU under load
+            step(bufs[0])
+        barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for k in range(args.steps):
+        step(bufs[k % nbuf])
+    t1.record()
+    barrier()
+    ms = t0.elapsed_time(t1)
+    if clocks:
+        t_load = time.perf_counter() + 0.3
+        while time.perf_counter() < t_load:
+            step(bufs[0])
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = b * world * args.steps / (ms / 1e3)
+
+    # ---- kernel-only timing of the solve launch (roofline) ----------------
+    stats = torch.empty(2, dtype=torch.int32, device=dev)
+    x0 = bufs[0]
+    out = torch.empty(b, n, dtype=torch.long, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    lib.tm_jv_stats_f32(x0.data_ptr(), x0.numel(), stats.data_ptr(), stream)
+    flags, key = (int(v) & 0xFFFFFFFF for v in stats.cpu().tolist())
+    sentinel, pinf = sharded.sentinel_from_words(sharded.stats_words(flags, key), max(n, m))
+    reps = max(3, min(args.steps, 50))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(reps)]
+    sevs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(reps)]
+    for r in range(reps):
+        x = bufs[r % nbuf]
+        sevs[r][0].record()
+        lib.tm_jv_stats_f32(x.data_ptr(), x.numel(), stats.data_ptr(), stream)
+        sevs[r][1].record()
+        evs[r][0].record()
+        rc = lib.tm_jv_solve_f32(x.data_ptr(), b, n, m, sentinel, int(pinf), out.data_ptr(),
+                                 None, stream)
+        evs[r][1].record()
+        assert rc == 0, lib.tm_status_string(rc)
+    torch.cuda.synchronize()
+    solve_ms = statistics.mean(a.elapsed_time(z) for a, z in evs)
+    stats_ms = statistics.mean(a.elapsed_time(z) for a, z in sevs)
+    alg_bytes = b * (n * m * 4 + n * 8)
+    achieved = alg_bytes / (solve_ms / 1e3) / 1e9
+    peak, peak_src = peak_hbm()
+
+    # ---- end to end: pinned host batch in, mapping out ---------------------
+    host = make_batch(args.config, min(b, 8192), 7).pin_memory() if args.config != "c5" else \
+        bufs[0][: min(b, 4096)].cpu().pin_memory()
+    eb = host.shape[0]
+    e_steps = max(3, min(args.steps, 20))
+    op(host.to(dev, non_blocking=True)).cpu()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e_steps):
+        xd = host.to(dev, non_blocking=True)
+        res = step(xd).cpu()
+    e1.record()
+    barrier()
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e = {"value": eb * world * e_steps / (e_ms / 1e3), "unit": UNIT,
+           "h2d_bytes_per_step": host.numel() * 4 * world,
+           "d2h_bytes_per_step": res.numel() * 8 * world,
+           "problems_per_step": eb * world}
+
+    base = cpu_baseline(args.config) if (rank == 0 and world == 1) else None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": spec["desc"], "global_batch": b * world, "per_gpu_batch": b,
+                       "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
+                       "l2": f"{nbuf} rotating input copies of {per_bytes / 2**20:.0f} MiB "
+                             f"(> 2x L2) so each step reads HBM"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic_for(args.config),
+                         "kernel": "jv_batch_kernel", "avg_launch_us": solve_ms * 1e3,
+                         "alg_bytes_per_launch": alg_bytes, "peak_source": peak_src,
+                         "stats_kernel_avg_us": stats_ms * 1e3,
+                         "op_roofline_frac": (alg_bytes / (ms / args.steps / 1e3) / 1e9) / peak},
+            "cpu_baseline": base,
+            "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk if clocks else None,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,109 @@
+/*
+ * torchmatch_b200 -- C ABI of the B200 (sm_100a) batched Jonker-Volgenant
+ * solver.
+ *
+ * These entry points replace the CUDA side of the reference's
+ * torch.ops.assignment.jonker_dense_batch (tue-p8n/torchmatch 1.0.3,
+ * sources/torchmatch/assignment/):
+ *
+ *   tm_jv_stats_f32         replaces k_scan_sentinel_stats + the scan half of
+ *                           compute_inf_sentinel  (cuda/cuda_common.cuh:186-243)
+ *   tm_jv_sentinel          replaces the check + formula half of
+ *                           compute_inf_sentinel  (cuda/cuda_common.cuh:245-254,
+ *                           cpu/ops.cpp:86-92)
+ *   tm_jv_solve_f32         replaces rewrite_inf_to_sentinel + the batched
+ *                           kernel launch          (cuda/cuda_common.cuh:270-284,
+ *                           cuda/jonker_tiled.cuh:203-218,
+ *                           cuda/dispatch.cu:156-176); the result follows the
+ *                           CPU solver (cpu/ops.cpp:176-289 +
+ *                           cpu/jonker_dense_flat.h:124-274) bit for bit
+ *   tm_jonker_dense_batch_f32  the whole op body of jonker_dense_batch_cuda
+ *                           (cuda/dispatch.cu:137-177) for callers without
+ *                           torch: stats, host check, solve
+ *
+ * Conventions: plain device pointers and sizes, no torch types, no C++
+ * exceptions.  Every function returns a tm_status code; CUDA errors are
+ * reported as TM_ERR_CUDA and the cudaError_t is kept for tm_last_cuda_error().
+ * All work is enqueued on the given stream; only tm_jonker_dense_batch_f32
+ * synchronises it (to read the NaN / -inf verdict, as the reference does).
+ */
+#ifndef TORCHMATCH_B200_H
+#define TORCHMATCH_B200_H
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *tm_stream_t; /* == cudaStream_t */
+
+typedef enum tm_status {
+    TM_OK = 0,
+    TM_ERR_NAN = 1,        /* a cell is NaN ("cost matrix contains NaN")      */
+    TM_ERR_NEG_INF = 2,    /* a cell is -inf ("cost matrix contains -inf")    */
+    TM_ERR_ARG = 3,        /* bad shape / null pointer / unsupported size     */
+    TM_ERR_CUDA = 4,       /* a CUDA call failed; see tm_last_cuda_error()    */
+    TM_ERR_TOO_LARGE = 5,  /* max(N, M) above tm_jv_max_k()                    */
+    TM_ERR_UNSOLVED = 6    /* a problem hit a loop bound; its row is all -1    */
+} tm_status;
+
+/* Batch statistics, device-resident.  Written by tm_jv_stats_f32. */
+typedef struct tm_jv_stats {
+    uint32_t flags;     /* TM_STAT_* bits                                    */
+    uint32_t max_key;   /* order-preserving key of the largest finite cell   */
+} tm_jv_stats;
+
+#define TM_STAT_NAN      1u
+#define TM_STAT_NEG_INF  2u
+#define TM_STAT_FINITE   4u
+#define TM_STAT_POS_INF  8u
+
+/* Largest max(N, M) the solver accepts. */
+int tm_jv_max_k(void);
+
+/* Scans `count` fp32 cells once and writes the batch statistics to
+ * `stats_dev` (zeroed by this call first).  Replaces
+ * cuda/cuda_common.cuh:186-243 (k_scan_sentinel_stats). */
+int tm_jv_stats_f32(const float *costs, int64_t count, tm_jv_stats *stats_dev,
+                    tm_stream_t stream);
+
+/* Host side: checks a copied-back tm_jv_stats and returns the +inf
+ * sentinel (max_finite + 1) * (K + 1), or 1 when no cell is finite.
+ * Returns TM_ERR_NAN / TM_ERR_NEG_INF like cuda/cuda_common.cuh:245-249.
+ * `has_pos_inf` (may be NULL) tells whether any +inf cell exists. */
+int tm_jv_sentinel(const tm_jv_stats *stats_host, int K, float *sentinel,
+                   int *has_pos_inf);
+
+/* Solves B problems of shape (N, M), costs contiguous fp32 (B, N, M),
+ * into out (B, N) int64 (row -> column, -1 = unmatched).  `sentinel`
+ * replaces +inf cells (only read when has_pos_inf != 0).  `status_dev`
+ * (may be NULL) is a device int32 that receives TM_ERR_UNSOLVED via
+ * atomicOr if any problem hits a loop bound; the caller zeroes it.
+ * Replaces cuda/cuda_common.cuh:270-284 + cuda/jonker_tiled.cuh:203-218. */
+int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
+                    int has_pos_inf, int64_t *out, int32_t *status_dev,
+                    tm_stream_t stream);
+
+/* Device scratch needed by tm_jonker_dense_batch_f32 (bytes). */
+size_t tm_jv_workspace_bytes(void);
+
+/* The whole jonker_dense_batch op for a caller without torch: statistics,
+ * one stream synchronisation for the NaN / -inf verdict, solve.  `workspace`
+ * is device memory of tm_jv_workspace_bytes().  Replaces
+ * cuda/dispatch.cu:137-177 (jonker_dense_batch_cuda). */
+int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M,
+                              int64_t *out, void *workspace, tm_stream_t stream);
+
+/* The cudaError_t of the last TM_ERR_CUDA on this thread. */
+int tm_last_cuda_error(void);
+
+/* Human-readable text for a tm_status code. */
+const char *tm_status_string(int status);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TORCHMATCH_B200_H */

@@ -1,0 +1,87 @@
+"""TEST INFRASTRUCTURE ONLY: ctypes bindings of the CPU oracle.
+
+``jonker_dense_batch`` runs ``jv_oracle.c`` (this repository's C restatement of
+the reference's CPU path, cpu/ops.cpp:176-289 + cpu/jonker_dense_flat.h).
+``reference_jonker_dense_batch`` runs the reference's own solver core compiled
+from its sources into ``oracle/_ref/`` (absent where the reference tree was
+never available to build it).  Only tests, ``__graft_entry__.smoke()`` and
+bench.py's CPU-baseline leg import this module.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "libtmoracle.so"
+REF_LIB = HERE / "_ref" / "libtmref.so"
+
+_ERRORS = {
+    1: "jonker: cost matrix contains NaN. Use +inf for forbidden pairs",
+    2: "jonker: cost matrix contains -inf. Use +inf for forbidden pairs",
+    3: "jonker oracle: allocation failure",
+}
+
+
+def build() -> None:
+    """Compile the oracle (and oracle/_ref where the reference tree exists)."""
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+
+
+def _load(path: Path, symbol: str):
+    if not path.exists():
+        raise FileNotFoundError(f"{path} is not built (run make -C {HERE})")
+    lib = ctypes.CDLL(str(path))
+    fn = getattr(lib, symbol)
+    fn.restype = ctypes.c_int
+    fn.argtypes = [
+        ctypes.c_void_p,
+        ctypes.c_int64,
+        ctypes.c_int,
+        ctypes.c_int,
+        ctypes.c_void_p,
+        ctypes.c_int,
+    ]
+    return fn
+
+
+_fns: dict[str, object] = {}
+
+
+def _call(path: Path, symbol: str, costs, threads: int) -> np.ndarray:
+    key = f"{path}:{symbol}"
+    if key not in _fns:
+        _fns[key] = _load(path, symbol)
+    fn = _fns[key]
+    a = np.ascontiguousarray(np.asarray(costs, dtype=np.float32))
+    if a.ndim != 3:
+        raise ValueError("costs must be 3D (B, N, M)")
+    b, n, m = a.shape
+    out = np.full((b, n), -1, dtype=np.int64)
+    rc = fn(a.ctypes.data, b, n, m, out.ctypes.data, int(threads))
+    if rc != 0:
+        raise RuntimeError(_ERRORS.get(rc, f"oracle failed with code {rc}"))
+    return out
+
+
+def jonker_dense_batch(costs, threads: int = 0) -> np.ndarray:
+    """Oracle restatement: (B, N, M) float32 -> (B, N) int64, -1 = unmatched."""
+    return _call(LIB, "tmo_jonker_dense_batch_f32", costs, threads)
+
+
+def reference_available() -> bool:
+    return REF_LIB.exists()
+
+
+def reference_jonker_dense_batch(costs, threads: int = 0) -> np.ndarray:
+    """The reference's compiled solver core behind the same batch driver."""
+    return _call(REF_LIB, "tmref_jonker_dense_batch_f32", costs, threads)
+
+
+def host_threads() -> int:
+    return len(os.sched_getaffinity(0))

@@ -1,0 +1,97 @@
+"""Loads the native libraries and wires ``torch.ops.assignment.jonker_dense_batch``.
+
+Mirrors the role of the reference loaders (tue-p8n/torchmatch 1.0.3,
+sources/torchmatch/assignment/_loader.py:111-169, _cpu.py:58-74,
+_cuda.py:54-73) for the one operator this package provides:
+
+* the schema ``assignment::jonker_dense_batch(Tensor costs) -> Tensor`` is
+  defined here unless the reference's CPU extension already defined it
+  (cpu/ops.cpp:486-496 owns it when both are loaded; load it first);
+* the fake kernel ``(B, N, M) -> (B, N) int64`` (_loader.py:160-169) is
+  registered unless one exists;
+* ``lib/libtmjv_torch.so`` registers the CUDA kernel.
+
+There is no fallback: if the library is missing or fails to load, importing
+raises, so a GPU run can never silently take another path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import functools
+from pathlib import Path
+
+import torch
+
+PKG = Path(__file__).resolve().parent
+LIBDIR = PKG / "lib"
+CORE_LIB = LIBDIR / "libtmjv.so"
+TORCH_LIB = LIBDIR / "libtmjv_torch.so"
+
+OP = "assignment::jonker_dense_batch"
+SCHEMA = "(Tensor costs) -> Tensor"
+
+_LIB_HANDLES: list[object] = []
+
+
+def _has_op() -> bool:
+    try:
+        torch._C._dispatch_find_schema_or_throw(OP, "")
+        return True
+    except RuntimeError:
+        return False
+
+
+def _fake(costs: torch.Tensor) -> torch.Tensor:
+    torch._check(costs.dim() == 3, lambda: "costs must be 3D (B, N, M)")
+    return costs.new_empty(costs.size(0), costs.size(1), dtype=torch.long)
+
+
+@functools.cache
+def load() -> None:
+    """Define the op (if needed), register its fake and load the CUDA impl."""
+    if not TORCH_LIB.exists():
+        raise ImportError(
+            f"{TORCH_LIB} is not built; run `python -m torchmatch_b200._build`"
+        )
+    if not _has_op():
+        lib = torch.library.Library("assignment", "FRAGMENT")
+        lib.define("jonker_dense_batch" + SCHEMA)
+        _LIB_HANDLES.append(lib)
+    try:
+        torch.library.register_fake(OP)(_fake)
+    except RuntimeError:
+        pass  # the reference's loader registered the same fake already
+    torch.ops.load_library(str(TORCH_LIB))
+
+
+@functools.cache
+def core() -> ctypes.CDLL:
+    """The plain C ABI (include/torchmatch_b200.h) through ctypes."""
+    lib = ctypes.CDLL(str(CORE_LIB))
+    i64, i32, vp = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
+    lib.tm_jv_max_k.restype = i32
+    lib.tm_jv_stats_f32.argtypes = [vp, i64, vp, vp]
+    lib.tm_jv_sentinel.argtypes = [vp, i32, vp, vp]
+    lib.tm_jv_solve_f32.argtypes = [vp, i64, i32, i32, ctypes.c_float, i32, vp, vp, vp]
+    lib.tm_jv_workspace_bytes.restype = ctypes.c_size_t
+    lib.tm_jonker_dense_batch_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
+    lib.tm_status_string.restype = ctypes.c_char_p
+    lib.tm_status_string.argtypes = [i32]
+    for name in ("tm_jv_stats_f32", "tm_jv_sentinel", "tm_jv_solve_f32",
+                 "tm_jonker_dense_batch_f32", "tm_last_cuda_error"):
+        getattr(lib, name).restype = i32
+    return lib
+
+
+# Every symbol include/torchmatch_b200.h declares.
+EXPORTED = (
+    "tm_jv_max_k",
+    "tm_jv_stats_f32",
+    "tm_jv_sentinel",
+    "tm_jv_solve_f32",
+    "tm_jv_workspace_bytes",
+    "tm_jonker_dense_batch_f32",
+    "tm_last_cuda_error",
+    "tm_status_string",
+)

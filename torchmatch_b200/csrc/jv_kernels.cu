@@ -1,0 +1,977 @@
+// Batched Jonker-Volgenant (LAPJV) for B200 / sm_100a.
+//
+// One warp owns one problem at a time.  Lane `l` owns the columns
+// col(s, l) = (s / VEC) * 32 * VEC + l * VEC + s % VEC for slots s < S, so a
+// row of the cost matrix is one (or S / VEC vectorised) conflict-free load
+// per lane and every reduction over a row is a single warp reduction
+// (redux.sync on fp32, new with sm_100a).  Column prices v and Dijkstra
+// distances d live in registers of the owning lane; the row-indexed arrays
+// (x, free-row queue) and the column permutation of the Dijkstra phase live
+// in a small per-warp shared-memory block.
+//
+// Two storage modes for the cost matrix:
+//   TILE = true   the (N, M) block of the problem is staged into shared
+//                 memory by one TMA bulk copy (cp.async.bulk + mbarrier)
+//                 and rows are read from there; the next problem is
+//                 prefetched into L2 while the current one is solved.
+//   TILE = false  for matrices that do not fit next to enough warps, rows
+//                 are streamed from L2/HBM with read-only vector loads.
+//
+// Algorithm: the reference's CPU solver, reproduced step for step so the
+// mapping is identical on every input, ties included
+// (sources/torchmatch/assignment/cpu/jonker_dense_flat.h, tue-p8n/torchmatch
+// 1.0.3):
+//   column reduction + reduction transfer      :124-176
+//   augmenting row reduction (two passes)       :178-235, :265-269
+//   shortest augmenting path + augmentation     :27-122, :237-258
+// and the batch driver of cpu/ops.cpp:176-289 (virtual zero padding to
+// K = max(N, M), +inf -> batch-global sentinel, column >= M -> -1).
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "torchmatch_b200.h"
+
+namespace tmjv {
+
+constexpr float kBig = 1e18f;  // LARGE_V<float>, jonker_dense_flat.h:22-23
+constexpr unsigned kFull = 0xffffffffu;
+constexpr int kMaxSlots = 8;   // K <= 256
+constexpr uint32_t kWaitLimit = 1u << 26;  // bounded mbarrier wait
+
+struct Params {
+    const float *costs;
+    int64_t B;
+    int N, M, K;
+    float sentinel;
+    int sanitize;        // batch holds +inf cells
+    int64_t *out;
+    int32_t *status;
+    int warp_bytes;      // shared-memory bytes per warp
+    int tile_floats;     // floats reserved for the staged tile (TILE mode)
+    int bulk_ok;         // tile base and size are 16-byte multiples
+};
+
+// ---------------------------------------------------------------- warp ops
+__device__ __forceinline__ float warp_min_f(float x) {
+    float r;
+    asm volatile("redux.sync.min.f32 %0, %1, %2;" : "=f"(r) : "f"(x), "r"(kFull));
+    return r;
+}
+__device__ __forceinline__ unsigned warp_min_u(unsigned x) {
+    return __reduce_min_sync(kFull, x);
+}
+__device__ __forceinline__ int warp_max_i(int x) { return __reduce_max_sync(kFull, x); }
+
+template <int S, int VEC>
+struct Layout {
+    static_assert(S % VEC == 0, "slots must be a multiple of the vector width");
+    __device__ static __forceinline__ int col(int s, int lane) {
+        return (s / VEC) * (32 * VEC) + lane * VEC + (s % VEC);
+    }
+    __device__ static __forceinline__ int lane_of(int j) { return (j % (32 * VEC)) / VEC; }
+    __device__ static __forceinline__ int slot_of(int j) {
+        return (j / (32 * VEC)) * VEC + (j % VEC);
+    }
+};
+
+// Select a[s] for a warp-uniform runtime slot without local-memory indexing.
+template <int S>
+__device__ __forceinline__ float sel(const float (&a)[S], int s) {
+    float r = a[0];
+#pragma unroll
+    for (int t = 1; t < S; ++t)
+        if (s == t) r = a[t];
+    return r;
+}
+
+// --------------------------------------------------------------- smem view
+struct WarpShared {
+    float *tile;       // staged (N, M) cost block (TILE mode)
+    float *dist;       // d, mirrored for position-ordered access
+    int32_t *xrow;     // x: column of each row
+    int16_t *ycol;     // y: row of each column
+    int16_t *pred;     // predecessor row of each column
+    int16_t *queue;    // free-row queue
+    int16_t *order;    // column permutation of the Dijkstra phase
+    uint8_t *flag;     // per-row "single" bit / per-column event bits
+    uint64_t *bar;     // mbarrier of the tile copy
+};
+
+__host__ __device__ inline int slots_for(int K) { return (K + 31) / 32; }
+
+// Per-warp shared bytes: bookkeeping arrays for KP = 32 * S entries.
+__host__ __device__ inline int book_bytes(int KP) {
+    return KP * 4 /*dist*/ + KP * 4 /*xrow*/ + KP * 2 * 4 /*ycol,pred,queue,order*/ +
+           KP /*flag*/ + 16 /*bar*/;
+}
+
+__device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP) {
+    WarpShared w;
+    unsigned char *p = base;
+    w.tile = reinterpret_cast<float *>(p);
+    p += (size_t)tile_floats * 4;
+    w.dist = reinterpret_cast<float *>(p); p += KP * 4;
+    w.xrow = reinterpret_cast<int32_t *>(p); p += KP * 4;
+    w.ycol = reinterpret_cast<int16_t *>(p); p += KP * 2;
+    w.pred = reinterpret_cast<int16_t *>(p); p += KP * 2;
+    w.queue = reinterpret_cast<int16_t *>(p); p += KP * 2;
+    w.order = reinterpret_cast<int16_t *>(p); p += KP * 2;
+    w.flag = p; p += KP;
+    p = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
+    w.bar = reinterpret_cast<uint64_t *>(p);
+    return w;
+}
+
+// ------------------------------------------------------------ row access
+// Reads row i of the virtual K x K matrix: real cells from `src` (row
+// stride M), zeros in the padding (cpu/ops.cpp:262-270).  In streaming mode
+// +inf cells become the sentinel here; in TILE mode the tile was already
+// sanitised.
+template <int S, int VEC, bool TILE>
+__device__ __forceinline__ void load_row(const float *__restrict__ src, int i, int N, int M,
+                                         int lane, bool sanitize, float sentinel,
+                                         float (&c)[S]) {
+    using L = Layout<S, VEC>;
+    if (i >= N) {
+#pragma unroll
+        for (int s = 0; s < S; ++s) c[s] = 0.0f;
+        return;
+    }
+    const float *row = src + (size_t)i * M;
+#pragma unroll
+    for (int g = 0; g < S / VEC; ++g) {
+        const int j0 = L::col(g * VEC, lane);
+        if (j0 + VEC <= M) {
+            if constexpr (VEC == 4) {
+                float4 t;
+                if constexpr (TILE) t = *reinterpret_cast<const float4 *>(row + j0);
+                else t = __ldg(reinterpret_cast<const float4 *>(row + j0));
+                c[g * 4 + 0] = t.x; c[g * 4 + 1] = t.y; c[g * 4 + 2] = t.z; c[g * 4 + 3] = t.w;
+            } else if constexpr (VEC == 2) {
+                float2 t;
+                if constexpr (TILE) t = *reinterpret_cast<const float2 *>(row + j0);
+                else t = __ldg(reinterpret_cast<const float2 *>(row + j0));
+                c[g * 2 + 0] = t.x; c[g * 2 + 1] = t.y;
+            } else {
+                if constexpr (TILE) c[g] = row[j0];
+                else c[g] = __ldg(row + j0);
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) {
+                const int j = j0 + e;
+                float val = 0.0f;
+                if (j < M) {
+                    if constexpr (TILE) val = row[j];
+                    else val = __ldg(row + j);
+                }
+                c[g * VEC + e] = val;
+            }
+        }
+    }
+    if constexpr (!TILE) {
+        if (sanitize) {
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+                if (isinf(c[s])) c[s] = sentinel;
+        }
+    }
+}
+
+// ------------------------------------------------------------- one solve
+template <int S, int VEC, bool TILE>
+__device__ void solve_problem(const float *__restrict__ src, const Params &P, WarpShared &w,
+                              int lane, int64_t b) {
+    using L = Layout<S, VEC>;
+    const int K = P.K, N = P.N, M = P.M;
+    const bool sanitize = P.sanitize != 0;
+    const float sentinel = P.sentinel;
+    constexpr int KP = 32 * S;
+    (void)KP;
+
+    int jj[S];
+    unsigned valid = 0;
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        jj[s] = L::col(s, lane);
+        if (jj[s] < K) valid |= 1u << s;
+    }
+
+    float v[S], d[S], c[S];
+    bool failed = false;
+
+    // ---- column reduction (jonker_dense_flat.h:129-144) -------------------
+    int ymin[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) { v[s] = kBig; ymin[s] = 0; }
+    {
+        const int nreal = N < K ? N : K;
+        int i = 0;
+        for (; i + 2 <= nreal; i += 2) {
+            float c0[S], c1[S];
+            load_row<S, VEC, TILE>(src, i, N, M, lane, sanitize, sentinel, c0);
+            load_row<S, VEC, TILE>(src, i + 1, N, M, lane, sanitize, sentinel, c1);
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
+                if (c0[s] < v[s]) { v[s] = c0[s]; ymin[s] = i; }
+                if (c1[s] < v[s]) { v[s] = c1[s]; ymin[s] = i + 1; }
+            }
+        }
+        for (; i < nreal; ++i) {
+            load_row<S, VEC, TILE>(src, i, N, M, lane, sanitize, sentinel, c);
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+                if (c[s] < v[s]) { v[s] = c[s]; ymin[s] = i; }
+        }
+        if (N < K) {  // first all-zero padding row; later ones never win (<)
+#pragma unroll
+            for (int s = 0; s < S; ++s)
+                if (0.0f < v[s]) { v[s] = 0.0f; ymin[s] = N; }
+        }
+    }
+
+    // ---- claim: highest column wins its row (:145-155) -------------------
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        const int r = s * 32 + lane;
+        if (r < K) { w.xrow[r] = -1; w.flag[r] = 1; }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+        if (valid >> s & 1) atomicMax(&w.xrow[ymin[s]], jj[s]);
+    __syncwarp();
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        if (valid >> s & 1) {
+            const int r = ymin[s];
+            int yv = r;
+            if (w.xrow[r] != jj[s]) { w.flag[r] = 0; yv = -1; }
+            w.ycol[jj[s]] = (int16_t)yv;
+        }
+    }
+    __syncwarp();
+
+    // ---- free-row list and reduction transfer (:157-174) ------------------
+    int nfree = 0;
+    unsigned single_mask[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        const int r = s * 32 + lane;
+        const int xr = r < K ? w.xrow[r] : 0;
+        const bool isfree = r < K && xr < 0;
+        const bool single = r < K && xr >= 0 && w.flag[r];
+        const unsigned bf = __ballot_sync(kFull, isfree);
+        single_mask[s] = __ballot_sync(kFull, single);
+        if (isfree) w.queue[nfree + __popc(bf & ((1u << lane) - 1))] = (int16_t)r;
+        nfree += __popc(bf);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        unsigned m = single_mask[s];
+        while (m) {
+            const int l = __ffs(m) - 1;
+            m &= m - 1;
+            const int i = s * 32 + l;
+            const int own = w.xrow[i];
+            load_row<S, VEC, TILE>(src, i, N, M, lane, sanitize, sentinel, c);
+            float loc = kBig;
+#pragma unroll
+            for (int t = 0; t < S; ++t)
+                if ((valid >> t & 1) && jj[t] != own) loc = fminf(loc, c[t] - v[t]);
+            const float mn = warp_min_f(loc);
+            if (lane == L::lane_of(own)) {
+                const int so = L::slot_of(own);
+#pragma unroll
+                for (int t = 0; t < S; ++t)
+                    if (t == so) v[t] -= mn;
+            }
+        }
+    }
+    // flags now serve as per-column event bits; they start cleared
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        const int r = s * 32 + lane;
+        if (r < K) w.flag[r] = 0;
+    }
+    __syncwarp();
+
+    // ---- augmenting row reduction, at most two passes (:178-235) ----------
+    for (int pass = 0; pass < 2 && nfree > 0 && !failed; ++pass) {
+        unsigned head = 0, visits = 0;
+        int kept = 0;
+        const unsigned cap = (unsigned)K * (unsigned)K + 2u * K + 8u;
+        while (head < (unsigned)nfree) {
+            if (++visits > cap) { failed = true; break; }
+            const int row = w.queue[head];
+            ++head;
+            load_row<S, VEC, TILE>(src, row, N, M, lane, sanitize, sentinel, c);
+            float r[S];
+            float loc = __int_as_float(0x7f800000);
+            bool big = false;
+#pragma unroll
+            for (int s = 0; s < S; ++s) {
+                r[s] = c[s] - v[s];
+                if (valid >> s & 1) {
+                    loc = fminf(loc, r[s]);
+                    big |= !(r[s] < kBig);
+                }
+            }
+            int j1, j2;
+            float v1, v2;
+            if (!__any_sync(kFull, big)) {
+                // all reduced costs below LARGE: the reference's two-min scan
+                // is the lexicographic (value, column) top-2
+                v1 = warp_min_f(loc);
+                unsigned cand = 0xffffffffu;
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if ((valid >> s & 1) && r[s] == v1) cand = min(cand, (unsigned)jj[s]);
+                j1 = (int)warp_min_u(cand);
+                float loc2 = __int_as_float(0x7f800000);
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if ((valid >> s & 1) && jj[s] != j1) loc2 = fminf(loc2, r[s]);
+                if (K > 1) {
+                    v2 = warp_min_f(loc2);
+                    unsigned cand2 = 0xffffffffu;
+#pragma unroll
+                    for (int s = 0; s < S; ++s)
+                        if ((valid >> s & 1) && jj[s] != j1 && r[s] == v2)
+                            cand2 = min(cand2, (unsigned)jj[s]);
+                    j2 = (int)warp_min_u(cand2);
+                } else {
+                    v2 = kBig;
+                    j2 = -1;
+                }
+            } else {
+                // rare: costs near LARGE -- replay the scalar scan exactly
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if (valid >> s & 1) w.dist[jj[s]] = r[s];
+                __syncwarp();
+                int a = 0, bb = -1;
+                float va = 0.0f, vb = kBig;
+                if (lane == 0) {
+                    va = w.dist[0];
+                    for (int j = 1; j < K; ++j) {
+                        const float t = w.dist[j];
+                        if (t < vb) {
+                            if (t >= va) { vb = t; bb = j; }
+                            else { vb = va; bb = a; va = t; a = j; }
+                        }
+                    }
+                }
+                j1 = __shfl_sync(kFull, a, 0);
+                j2 = __shfl_sync(kFull, bb, 0);
+                v1 = __shfl_sync(kFull, va, 0);
+                v2 = __shfl_sync(kFull, vb, 0);
+                __syncwarp();
+            }
+            int i0 = w.ycol[j1];
+            const float vj1 = __shfl_sync(kFull, sel(v, L::slot_of(j1)), L::lane_of(j1));
+            const float lowered = vj1 - (v2 - v1);
+            const bool lowers = lowered < vj1;
+            int jsel = j1;
+            int push_front = -1, push_back = -1;
+            if (visits < head * (unsigned)K) {
+                if (lowers) {
+                    if (lane == L::lane_of(j1)) {
+                        const int so = L::slot_of(j1);
+#pragma unroll
+                        for (int t = 0; t < S; ++t)
+                            if (t == so) v[t] = lowered;
+                    }
+                } else if (i0 >= 0 && j2 >= 0) {
+                    jsel = j2;
+                    i0 = w.ycol[j2];
+                }
+                if (i0 >= 0) {
+                    if (lowers) push_front = i0;
+                    else push_back = i0;
+                }
+            } else if (i0 >= 0) {
+                push_back = i0;
+            }
+            __syncwarp();
+            if (push_front >= 0) --head;
+            if (lane == 0) {
+                if (push_front >= 0) w.queue[head] = (int16_t)push_front;
+                if (push_back >= 0) w.queue[kept] = (int16_t)push_back;
+                w.xrow[row] = jsel;
+                w.ycol[jsel] = (int16_t)row;
+            }
+            if (push_back >= 0) ++kept;
+            __syncwarp();
+        }
+        nfree = kept;
+    }
+
+    // ---- shortest augmenting paths (:75-122, :237-258) -------------------
+    for (int f = 0; f < nfree && !failed; ++f) {
+        const int start = w.queue[f];
+        load_row<S, VEC, TILE>(src, start, N, M, lane, sanitize, sentinel, c);
+        unsigned todo = valid, ready = 0, grp = 0;
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            d[s] = c[s] - v[s];
+            if (valid >> s & 1) {
+                w.dist[jj[s]] = d[s];
+                w.pred[jj[s]] = (int16_t)start;
+            }
+            const int p = s * 32 + lane;
+            if (p < K) w.order[p] = (int16_t)p;
+        }
+        __syncwarp();
+        int lo = 0, hi = 0, sink = -1, iter = 0;
+        float mind = 0.0f;
+        const int icap = 4 * K + 8;
+        while (sink < 0) {
+            if (++iter > icap) { failed = true; break; }
+            if (lo == hi) {
+                // -- minimum search with the reference's swap pattern (:27-43)
+                __syncwarp();
+                if (lo >= K) { failed = true; break; }
+                ready |= grp;
+                grp = 0;
+                float dv[S];
+                const float inf = __int_as_float(0x7f800000);
+#pragma unroll
+                for (int s = 0; s < S; ++s) {
+                    const int p = s * 32 + lane;
+                    dv[s] = inf;
+                    if (p >= lo && p < K) dv[s] = w.dist[w.order[p]];
+                }
+                float carry = inf;
+                unsigned evm[S], rsm[S];
+#pragma unroll
+                for (int s = 0; s < S; ++s) {
+                    const int p = s * 32 + lane;
+                    float incl = dv[s];
+#pragma unroll
+                    for (int off = 1; off < 32; off <<= 1) {
+                        const float t = __shfl_up_sync(kFull, incl, off);
+                        if (lane >= off) incl = fminf(incl, t);
+                    }
+                    float excl = __shfl_up_sync(kFull, incl, 1);
+                    excl = lane == 0 ? carry : fminf(carry, excl);
+                    const bool live = p > lo && p < K;
+                    const bool rst = live && dv[s] < excl;
+                    const bool tie = live && dv[s] == excl;
+                    rsm[s] = __ballot_sync(kFull, rst);
+                    evm[s] = __ballot_sync(kFull, rst || tie);
+                    carry = fminf(carry, __shfl_sync(kFull, incl, 31));
+                }
+                mind = carry;
+                int nh = lo + 1;
+                if (lane == 0) {
+#pragma unroll 1
+                    for (int s = 0; s < S; ++s) {
+                        unsigned m = evm[s];
+                        while (m) {
+                            const int l = __ffs(m) - 1;
+                            m &= m - 1;
+                            const int k = s * 32 + l;
+                            const int16_t e = w.order[k];
+                            if (rsm[s] >> l & 1) {
+                                w.order[k] = w.order[lo];
+                                w.order[lo] = e;
+                                nh = lo + 1;
+                            } else {
+                                w.order[k] = w.order[nh];
+                                w.order[nh] = e;
+                                ++nh;
+                            }
+                        }
+                    }
+                }
+                hi = __shfl_sync(kFull, nh, 0);
+                __syncwarp();
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if ((todo >> s & 1) && d[s] == mind) grp |= 1u << s;
+                todo &= ~grp;
+                // last free column of the group, in group order (:107-111)
+                int cand = -1;
+#pragma unroll
+                for (int s = 0; s < S; ++s) {
+                    const int p = s * 32 + lane;
+                    if (p >= lo && p < hi && w.ycol[w.order[p]] < 0) cand = p;
+                }
+                const int pbest = warp_max_i(cand);
+                if (pbest >= 0) {
+                    sink = w.order[pbest];
+                    break;
+                }
+            }
+            // -- relax the rows of the group, in group order (:45-73)
+            while (lo != hi) {
+                const int j = w.order[lo];
+                ++lo;
+                const int i = w.ycol[j];
+                const float dj = w.dist[j];
+                const int lj = L::lane_of(j), sj = L::slot_of(j);
+                const float vj = __shfl_sync(kFull, sel(v, sj), lj);
+                load_row<S, VEC, TILE>(src, i, N, M, lane, sanitize, sentinel, c);
+                const float cij = __shfl_sync(kFull, sel(c, sj), lj);
+                const float h = cij - vj - dj;
+                unsigned ev = 0;
+#pragma unroll
+                for (int s = 0; s < S; ++s) {
+                    if (todo >> s & 1) {
+                        const float rr = c[s] - v[s] - h;
+                        if (rr < d[s]) {
+                            d[s] = rr;
+                            w.dist[jj[s]] = rr;
+                            w.pred[jj[s]] = (int16_t)i;
+                            if (rr == dj) ev |= 1u << s;
+                        }
+                    }
+                }
+                if (!__any_sync(kFull, ev != 0)) continue;
+                // tie events: order them by position
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if (ev >> s & 1)
+                        w.flag[jj[s]] = (uint8_t)(1 | (w.ycol[jj[s]] < 0 ? 2 : 0));
+                __syncwarp();
+                unsigned em[S], fm[S];
+                int nev = 0;
+#pragma unroll
+                for (int s = 0; s < S; ++s) {
+                    const int p = s * 32 + lane;
+                    uint8_t fl = 0;
+                    if (p >= hi && p < K) fl = w.flag[w.order[p]];
+                    em[s] = __ballot_sync(kFull, fl & 1);
+                    fm[s] = __ballot_sync(kFull, fl & 2);
+                    nev += __popc(em[s]);
+                }
+                int first_free = -1;
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if (first_free < 0 && fm[s]) first_free = s * 32 + __ffs(fm[s]) - 1;
+                __syncwarp();
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if (ev >> s & 1) w.flag[jj[s]] = 0;
+                if (first_free >= 0) {
+                    sink = w.order[first_free];
+                    __syncwarp();
+                    break;
+                }
+                if (lane == 0) {
+                    int nh = hi;
+#pragma unroll 1
+                    for (int s = 0; s < S; ++s) {
+                        unsigned m = em[s];
+                        while (m) {
+                            const int l = __ffs(m) - 1;
+                            m &= m - 1;
+                            const int k = s * 32 + l;
+                            const int16_t e = w.order[k];
+                            w.order[k] = w.order[nh];
+                            w.order[nh] = e;
+                            ++nh;
+                        }
+                    }
+                }
+                hi += nev;
+                grp |= ev;
+                todo &= ~ev;
+                __syncwarp();
+            }
+        }
+        if (failed) break;
+        // price update of the settled columns (:117-119)
+#pragma unroll
+        for (int s = 0; s < S; ++s)
+            if (ready >> s & 1) v[s] += d[s] - mind;
+        // augmentation along the predecessor chain (:244-255)
+        if (lane == 0) {
+            int j = sink, steps = 0, i;
+            do {
+                i = w.pred[j];
+                w.ycol[j] = (int16_t)i;
+                const int prev = w.xrow[i];
+                w.xrow[i] = j;
+                j = prev;
+                if (++steps >= K) break;
+            } while (i != start);
+        }
+        __syncwarp();
+    }
+
+    // ---- output (cpu/ops.cpp:274-283) ------------------------------------
+    int64_t *ob = P.out + b * (int64_t)N;
+    for (int r = lane; r < N; r += 32) {
+        const int x = w.xrow[r];
+        ob[r] = (!failed && x >= 0 && x < M) ? (int64_t)x : (int64_t)-1;
+    }
+    if (failed && lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_ERR_UNSOLVED);
+    __syncwarp();
+}
+
+// --------------------------------------------------------- TMA primitives
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void bar_init(uint64_t *bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool bar_wait(uint64_t *bar, uint32_t phase) {
+    for (uint32_t it = 0; it < kWaitLimit; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
+            "selp.u32 %0, 1, 0, p; }"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(phase)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// ------------------------------------------------------------------ kernel
+template <int S, int VEC, bool TILE>
+__global__ void __launch_bounds__(512) jv_batch_kernel(const Params P) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const int lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
+    const int wpb = blockDim.x >> 5;
+    WarpShared w = carve(smem_raw + (size_t)warp * P.warp_bytes, TILE ? P.tile_floats : 0, 32 * S);
+    const int64_t per = (int64_t)P.N * P.M;
+    const uint32_t tile_bytes = (uint32_t)(per * 4);
+    uint32_t phase = 0;
+    if constexpr (TILE) {
+        if (lane == 0) bar_init(w.bar);
+        __syncwarp();
+    }
+    const int64_t stride = (int64_t)gridDim.x * wpb;
+    for (int64_t b = (int64_t)blockIdx.x * wpb + warp; b < P.B; b += stride) {
+        const float *g = P.costs + b * per;
+        const float *src = g;
+        if constexpr (TILE) {
+            bool ok = true;
+            if (P.bulk_ok) {
+                if (lane == 0) bulk_load(w.tile, g, tile_bytes, w.bar);
+                ok = bar_wait(w.bar, phase);
+                phase ^= 1u;
+            } else {
+                for (int64_t k = lane; k < per; k += 32) w.tile[k] = __ldg(g + k);
+            }
+            if (!__all_sync(kFull, ok)) {
+                if (lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_ERR_CUDA);
+                return;
+            }
+            if (P.sanitize) {
+                for (int64_t k = lane; k < per; k += 32)
+                    if (isinf(w.tile[k])) w.tile[k] = P.sentinel;
+            }
+            __syncwarp();
+            src = w.tile;
+            const int64_t nb = b + stride;
+            if (P.bulk_ok && lane == 0 && nb < P.B) prefetch_l2(P.costs + nb * per, tile_bytes);
+        }
+        solve_problem<S, VEC, TILE>(src, P, w, lane, b);
+    }
+}
+
+// ------------------------------------------------------------- statistics
+__device__ __forceinline__ uint32_t order_key(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__host__ __device__ inline float key_to_float(uint32_t k) {
+    const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(u);
+#else
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+#endif
+}
+
+__device__ __forceinline__ void classify(float x, uint32_t &fl, uint32_t &mk) {
+    if (isnan(x)) fl |= TM_STAT_NAN;
+    else if (isinf(x)) fl |= x < 0.0f ? TM_STAT_NEG_INF : TM_STAT_POS_INF;
+    else { fl |= TM_STAT_FINITE; mk = max(mk, order_key(x)); }
+}
+
+__global__ void __launch_bounds__(256) jv_stats_kernel(const float *__restrict__ x, int64_t n,
+                                                       tm_jv_stats *out) {
+    uint32_t fl = 0, mk = 0;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+    int64_t done = 0;
+    if (vec) {
+        const int64_t n4 = n / 4;
+        const float4 *x4 = reinterpret_cast<const float4 *>(x);
+        for (int64_t k = tid; k < n4; k += nth) {
+            const float4 t = __ldg(x4 + k);
+            classify(t.x, fl, mk); classify(t.y, fl, mk);
+            classify(t.z, fl, mk); classify(t.w, fl, mk);
+        }
+        done = n4 * 4;
+    }
+    for (int64_t k = done + tid; k < n; k += nth) classify(__ldg(x + k), fl, mk);
+    fl = __reduce_or_sync(kFull, fl);
+    mk = __reduce_max_sync(kFull, mk);
+    if ((threadIdx.x & 31) == 0) {
+        if (fl) atomicOr(&out->flags, fl);
+        if (mk) atomicMax(&out->max_key, mk);
+    }
+}
+
+// ------------------------------------------------------------ host launch
+static thread_local int g_last_cuda = 0;
+
+static int cuda_fail(cudaError_t e) {
+    g_last_cuda = (int)e;
+    return TM_ERR_CUDA;
+}
+
+// Makes the device that owns `stream` current for the scope of a call, so the
+// C ABI works whatever this runtime instance believes the current device is
+// (the library links its own static CUDA runtime).
+struct StreamDevice {
+    int prev = -1;
+    int dev = 0;
+    cudaError_t err = cudaSuccess;
+    explicit StreamDevice(cudaStream_t s) {
+        cudaGetDevice(&prev);
+        dev = prev;
+        if (s != nullptr) {
+            err = cudaStreamGetDevice(s, &dev);
+            if (err == cudaSuccess && dev != prev) err = cudaSetDevice(dev);
+        }
+    }
+    ~StreamDevice() {
+        if (prev >= 0 && dev != prev) cudaSetDevice(prev);
+    }
+};
+
+static int num_sms() {
+    static int sms[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!sms[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        sms[dev] = v > 0 ? v : 148;
+    }
+    return sms[dev];
+}
+
+constexpr int kSmemLimit = 227 * 1024;
+
+// Minimum number of resident warps per SM for the shared-memory tile mode
+// (TM_JV_TILE_MIN_WARPS overrides the default of 4; 0 disables the mode).
+static int tile_min_warps() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("TM_JV_TILE_MIN_WARPS");
+        v = e ? atoi(e) : 4;
+        if (v < 0) v = 4;
+    }
+    return v == 0 ? (1 << 20) : v;
+}
+constexpr int kMaxWarpsPerBlock = 16;
+
+template <int S, int VEC, bool TILE>
+static int launch_t(const Params &P0, cudaStream_t stream) {
+    Params P = P0;
+    const int KP = 32 * S;
+    int tile_floats = 0;
+    if (TILE) tile_floats = (int)(((int64_t)P.N * P.M + 31) / 32 * 32);
+    int warp_bytes = tile_floats * 4 + book_bytes(KP);
+    warp_bytes = (warp_bytes + 127) & ~127;
+    P.warp_bytes = warp_bytes;
+    P.tile_floats = tile_floats;
+    int wpb = kSmemLimit / warp_bytes;
+    if (wpb > kMaxWarpsPerBlock) wpb = kMaxWarpsPerBlock;
+    if (wpb < 1) return TM_ERR_TOO_LARGE;
+    const int64_t need_warps = P.B;
+    if ((int64_t)wpb > need_warps) wpb = (int)need_warps;
+    const int smem = wpb * warp_bytes;
+    auto kern = jv_batch_kernel<S, VEC, TILE>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_fail(e);
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (per_sm < 1) per_sm = 1;
+    int64_t blocks = (P.B + wpb - 1) / wpb;
+    const int64_t resident = (int64_t)num_sms() * per_sm;
+    if (blocks > resident) blocks = resident;
+    kern<<<(unsigned)blocks, wpb * 32, smem, stream>>>(P);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    return TM_OK;
+}
+
+// Picks the slot count, vector width and storage mode for a problem shape.
+static int launch(Params P, cudaStream_t stream) {
+    const int S = slots_for(P.K);
+    const uintptr_t base = reinterpret_cast<uintptr_t>(P.costs);
+    const int64_t per = (int64_t)P.N * P.M;
+    P.bulk_ok = ((base & 15) == 0) && ((per * 4) % 16 == 0);
+    // TILE mode while at least tile_min_warps() warps fit on one SM with
+    // their tiles; larger matrices stream their rows from L2/HBM.
+    const int64_t tile_bytes = ((per + 31) / 32 * 32) * 4 + book_bytes(32 * S);
+    const bool tile = tile_bytes * tile_min_warps() <= kSmemLimit;
+    const bool v4 = (P.M % 4 == 0) && (base % 16 == 0);
+    const bool v2 = (P.M % 2 == 0) && (base % 8 == 0);
+#define TM_L(SS, VV)                                                        \
+    return tile ? launch_t<SS, VV, true>(P, stream) : launch_t<SS, VV, false>(P, stream)
+    switch (S) {
+    case 1: TM_L(1, 1);
+    case 2: if (v2) { TM_L(2, 2); } TM_L(2, 1);
+    case 3: TM_L(3, 1);
+    case 4: if (v4) { TM_L(4, 4); } TM_L(4, 1);
+    case 5: TM_L(5, 1);
+    case 6: if (v2) { TM_L(6, 2); } TM_L(6, 1);
+    case 7: TM_L(7, 1);
+    case 8: if (v4) { TM_L(8, 4); } TM_L(8, 1);
+    default: return TM_ERR_TOO_LARGE;
+    }
+#undef TM_L
+}
+
+}  // namespace tmjv
+
+// ====================================================================== C ABI
+extern "C" {
+
+int tm_jv_max_k(void) { return 32 * tmjv::kMaxSlots; }
+
+int tm_last_cuda_error(void) { return tmjv::g_last_cuda; }
+
+const char *tm_status_string(int status) {
+    switch (status) {
+    case TM_OK: return "ok";
+    case TM_ERR_NAN:
+        return "cost matrix contains NaN; use +inf for forbidden pairs, NaN signals an upstream bug";
+    case TM_ERR_NEG_INF: return "cost matrix contains -inf; -inf has no forbidden-edge meaning";
+    case TM_ERR_ARG: return "invalid argument";
+    case TM_ERR_CUDA: return "batched JV kernel launch failed (CUDA error)";
+    case TM_ERR_TOO_LARGE: return "batched JV (CUDA) supports max(N, M) <= 256";
+    case TM_ERR_UNSOLVED: return "a problem exceeded the solver's loop bound";
+    default: return "unknown status";
+    }
+}
+
+int tm_jv_stats_f32(const float *costs, int64_t count, tm_jv_stats *stats_dev,
+                    tm_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (!stats_dev || count < 0 || (count > 0 && !costs)) return TM_ERR_ARG;
+    tmjv::StreamDevice scope(stream);
+    if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
+    cudaError_t e = cudaMemsetAsync(stats_dev, 0, sizeof(tm_jv_stats), stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    if (count == 0) return TM_OK;
+    const int threads = 256;
+    int64_t blocks = (count / 4 + threads - 1) / threads;
+    const int64_t cap = (int64_t)tmjv::num_sms() * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    tmjv::jv_stats_kernel<<<(unsigned)blocks, threads, 0, stream>>>(costs, count, stats_dev);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    return TM_OK;
+}
+
+int tm_jv_sentinel(const tm_jv_stats *st, int K, float *sentinel, int *has_pos_inf) {
+    if (!st || !sentinel) return TM_ERR_ARG;
+    if (st->flags & TM_STAT_NAN) return TM_ERR_NAN;
+    if (st->flags & TM_STAT_NEG_INF) return TM_ERR_NEG_INF;
+    if (has_pos_inf) *has_pos_inf = (st->flags & TM_STAT_POS_INF) ? 1 : 0;
+    if (!(st->flags & TM_STAT_FINITE)) {
+        *sentinel = 1.0f;
+    } else {
+        const float mx = tmjv::key_to_float(st->max_key);
+        volatile float k1 = (float)(K + 1);  // fp32 product, no contraction
+        *sentinel = (mx + 1.0f) * k1;
+    }
+    return TM_OK;
+}
+
+int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
+                    int has_pos_inf, int64_t *out, int32_t *status_dev, tm_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
+    if (B == 0 || N == 0) return TM_OK;
+    if (!out || (M > 0 && !costs)) return TM_ERR_ARG;
+    const int K = N > M ? N : M;
+    if (K > 32 * tmjv::kMaxSlots) return TM_ERR_TOO_LARGE;
+    tmjv::StreamDevice scope(stream);
+    if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
+    if (M == 0) {
+        cudaError_t e = cudaMemsetAsync(out, 0xff, sizeof(int64_t) * (size_t)B * N, stream);
+        return e == cudaSuccess ? TM_OK : tmjv::cuda_fail(e);
+    }
+    tmjv::Params P{};
+    P.costs = costs;
+    P.B = B;
+    P.N = N;
+    P.M = M;
+    P.K = K;
+    P.sentinel = sentinel;
+    P.sanitize = has_pos_inf ? 1 : 0;
+    P.out = out;
+    P.status = status_dev;
+    return tmjv::launch(P, stream);
+}
+
+size_t tm_jv_workspace_bytes(void) { return 256; }
+
+int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64_t *out,
+                              void *workspace, tm_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
+    if (B == 0 || N == 0) return TM_OK;
+    if (!out || !workspace) return TM_ERR_ARG;
+    tmjv::StreamDevice scope(stream);
+    if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
+    if (M == 0) return tm_jv_solve_f32(costs, B, N, M, 0.0f, 0, out, nullptr, stream_);
+    const int K = N > M ? N : M;
+    if (K > tm_jv_max_k()) return TM_ERR_TOO_LARGE;
+    tm_jv_stats *st = reinterpret_cast<tm_jv_stats *>(workspace);
+    int rc = tm_jv_stats_f32(costs, B * (int64_t)N * M, st, stream_);
+    if (rc) return rc;
+    tm_jv_stats h{};
+    cudaError_t e = cudaMemcpyAsync(&h, st, sizeof(h), cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    float sentinel = 1.0f;
+    int pinf = 0;
+    rc = tm_jv_sentinel(&h, K, &sentinel, &pinf);
+    if (rc) return rc;
+    return tm_jv_solve_f32(costs, B, N, M, sentinel, pinf, out, nullptr, stream_);
+}
+
+}  // extern "C"

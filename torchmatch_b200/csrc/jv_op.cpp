@@ -1,0 +1,98 @@
+// CUDA implementation of torch.ops.assignment.jonker_dense_batch.
+//
+// The operator schema "jonker_dense_batch(Tensor costs) -> Tensor" belongs to
+// the `assignment` library (tue-p8n/torchmatch 1.0.3,
+// sources/torchmatch/assignment/cpu/ops.cpp:486-496).  This file registers
+// only the CUDA kernel for it (the reference does the same in
+// cuda/dispatch.cu:181-186); the Python loader defines the schema and the
+// fake kernel when the reference's CPU extension has not done so already.
+//
+// Behaviour kept from jonker_dense_batch_cuda (cuda/dispatch.cu:137-177):
+// device guard, current-stream execution, refusal inside CUDA graph capture,
+// fp32 cast, batch-global +inf sentinel with a host sync to raise on NaN /
+// -inf, a fresh int64 (B, N) output.  Widened: rectangular (B, N, M) input
+// and max(N, M) up to tm_jv_max_k(); non-contiguous input is made
+// contiguous instead of rejected.  All device work goes through the C ABI in
+// include/torchmatch_b200.h.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <cuda_runtime.h>
+
+#include "torchmatch_b200.h"
+
+namespace {
+
+void check_not_capturing(cudaStream_t stream, const char *op_name) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    const cudaError_t e = cudaStreamIsCapturing(stream, &st);
+    TORCH_CHECK(e == cudaSuccess, "cudaStreamIsCapturing failed: ", cudaGetErrorString(e));
+    TORCH_CHECK(st == cudaStreamCaptureStatusNone, op_name,
+                " performs a host-side CUDA synchronization and cannot run inside CUDA "
+                "graph capture (e.g. torch.compile(mode=\"reduce-overhead\")); call it "
+                "outside the captured region.");
+}
+
+std::string status_text(int rc) {
+    std::string s = tm_status_string(rc);
+    if (rc == TM_ERR_CUDA) {
+        s += ": ";
+        s += cudaGetErrorString(static_cast<cudaError_t>(tm_last_cuda_error()));
+    }
+    return s;
+}
+
+at::Tensor jonker_dense_batch_cuda(const at::Tensor &costs) {
+    TORCH_CHECK(costs.is_cuda(), "costs must be a CUDA tensor");
+    TORCH_CHECK(costs.dim() == 3, "costs must be 3D (B, N, M), got ", costs.dim());
+    TORCH_CHECK(costs.scalar_type() == at::kFloat || costs.scalar_type() == at::kDouble,
+                "costs must be float32 or float64, got ", costs.scalar_type());
+    const c10::cuda::CUDAGuard guard(costs.device());
+
+    const int64_t B = costs.size(0);
+    const int64_t N = costs.size(1);
+    const int64_t M = costs.size(2);
+    if (B == 0 || N == 0 || M == 0)
+        return at::full({B, N}, -1, costs.options().dtype(at::kLong));
+    const int64_t K = std::max(N, M);
+    TORCH_CHECK(K <= tm_jv_max_k(), "Batched JV (CUDA) supports max(N, M) <= ", tm_jv_max_k(),
+                ", got K=", K);
+
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+    check_not_capturing(stream, "jonker_dense_batch");
+
+    const at::Tensor c = costs.to(at::kFloat).contiguous();
+    const float *cp = c.const_data_ptr<float>();
+    auto stream_h = reinterpret_cast<tm_stream_t>(stream);
+
+    at::Tensor stats = at::empty({(int64_t)sizeof(tm_jv_stats)}, c.options().dtype(at::kByte));
+    auto *st_dev = reinterpret_cast<tm_jv_stats *>(stats.mutable_data_ptr());
+    int rc = tm_jv_stats_f32(cp, c.numel(), st_dev, stream_h);
+    TORCH_CHECK(rc == TM_OK, "batched JV statistics failed: ", status_text(rc));
+    tm_jv_stats host{};
+    cudaError_t e =
+        cudaMemcpyAsync(&host, st_dev, sizeof(host), cudaMemcpyDeviceToHost, stream);
+    TORCH_CHECK(e == cudaSuccess, "batched JV statistics copy failed: ", cudaGetErrorString(e));
+    e = cudaStreamSynchronize(stream);
+    TORCH_CHECK(e == cudaSuccess, "batched JV statistics sync failed: ", cudaGetErrorString(e));
+    float sentinel = 1.0f;
+    int has_pos_inf = 0;
+    rc = tm_jv_sentinel(&host, static_cast<int>(K), &sentinel, &has_pos_inf);
+    TORCH_CHECK(rc != TM_ERR_NAN, "jonker_dense_batch: ", tm_status_string(rc));
+    TORCH_CHECK(rc != TM_ERR_NEG_INF, "jonker_dense_batch: ", tm_status_string(rc));
+    TORCH_CHECK(rc == TM_OK, "jonker_dense_batch: ", status_text(rc));
+
+    at::Tensor out = at::empty({B, N}, costs.options().dtype(at::kLong));
+    rc = tm_jv_solve_f32(cp, B, static_cast<int>(N), static_cast<int>(M), sentinel, has_pos_inf,
+                         out.mutable_data_ptr<int64_t>(), nullptr, stream_h);
+    TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
+    return out;
+}
+
+}  // namespace
+
+TORCH_LIBRARY_IMPL(assignment, CUDA, m) {
+    m.impl("jonker_dense_batch", &jonker_dense_batch_cuda);
+}
