@@ -7,7 +7,8 @@ Produces, next to this file:
 * ``lib/libtmjv_torch.so`` -- the ``TORCH_LIBRARY_IMPL(assignment, CUDA)``
   registration of ``jonker_dense_batch`` that calls into ``libtmjv.so``.
 
-Run ``python -m torchmatch_b200._build`` (``__graft_entry__.build()`` does).
+Run ``python torchmatch_b200/_build.py`` (``__graft_entry__.build()`` does); it is
+run by path because importing the package requires the built libraries.
 nvcc cross-compiles for sm_100a without a GPU present.
 """
 

@@ -52,7 +52,7 @@ def load() -> None:
     """Define the op (if needed), register its fake and load the CUDA impl."""
     if not TORCH_LIB.exists():
         raise ImportError(
-            f"{TORCH_LIB} is not built; run `python -m torchmatch_b200._build`"
+            f"{TORCH_LIB} is not built; run `python torchmatch_b200/_build.py`"
         )
     if not _has_op():
         lib = torch.library.Library("assignment", "FRAGMENT")
