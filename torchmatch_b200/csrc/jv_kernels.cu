@@ -41,6 +41,21 @@ constexpr unsigned kFull = 0xffffffffu;
 constexpr int kMaxSlots = 8;   // K <= 256
 constexpr uint32_t kWaitLimit = 1u << 26;  // bounded mbarrier wait
 
+// Optional per-phase cycle counters (build with -DTMJV_PHASE_CLOCKS; the
+// kernel then adds clock64() deltas into tmjv_phase_cycles[]).
+#ifdef TMJV_PHASE_CLOCKS
+__device__ unsigned long long tmjv_phase_cycles[8];
+#define TMJV_T(name) const long long name = clock64()
+#define TMJV_ACC(idx, t0)                                                            \
+    do {                                                                             \
+        if ((threadIdx.x & 31) == 0)                                                 \
+            atomicAdd(&tmjv_phase_cycles[idx], (unsigned long long)(clock64() - (t0))); \
+    } while (0)
+#else
+#define TMJV_T(name)
+#define TMJV_ACC(idx, t0)
+#endif
+
 struct Params {
     const float *costs;
     int64_t B;
@@ -87,6 +102,27 @@ __device__ __forceinline__ float sel(const float (&a)[S], int s) {
     return r;
 }
 
+template <int S>
+__device__ __forceinline__ int seli(const int (&a)[S], int s) {
+    int r = a[0];
+#pragma unroll
+    for (int t = 1; t < S; ++t)
+        if (s == t) r = a[t];
+    return r;
+}
+template <int S>
+__device__ __forceinline__ void setf(float (&a)[S], int s, float x) {
+#pragma unroll
+    for (int t = 0; t < S; ++t)
+        if (s == t) a[t] = x;
+}
+template <int S>
+__device__ __forceinline__ void seti(int (&a)[S], int s, int x) {
+#pragma unroll
+    for (int t = 0; t < S; ++t)
+        if (s == t) a[t] = x;
+}
+
 // --------------------------------------------------------------- smem view
 struct WarpShared {
     float *tile;       // staged (N, M) cost block (TILE mode)
@@ -98,17 +134,26 @@ struct WarpShared {
     int16_t *order;    // column permutation of the Dijkstra phase
     uint8_t *flag;     // per-row "single" bit / per-column event bits
     uint64_t *bar;     // mbarrier of the tile copy
+    // row cache of the augmenting row reduction (streaming mode only)
+    float2 *centry;    // [row][kCache]: {cost value, column as int bits}
+    float *cbound;     // [row]: lower bound of every uncached reduced cost
+    uint8_t *cflag;    // [row]: cache built
+    float *vsh;        // mirror of the prices v
 };
+
+constexpr int kCache = 4;  // cached columns per row
 
 __host__ __device__ inline int slots_for(int K) { return (K + 31) / 32; }
 
 // Per-warp shared bytes: bookkeeping arrays for KP = 32 * S entries.
-__host__ __device__ inline int book_bytes(int KP) {
-    return KP * 4 /*dist*/ + KP * 4 /*xrow*/ + KP * 2 * 4 /*ycol,pred,queue,order*/ +
-           KP /*flag*/ + 16 /*bar*/;
+__host__ __device__ inline int book_bytes(int KP, bool cache) {
+    int b = KP * 4 /*dist*/ + KP * 4 /*xrow*/ + KP * 2 * 4 /*ycol,pred,queue,order*/ +
+            KP /*flag*/ + 32 /*bar + alignment*/;
+    if (cache) b += KP * kCache * 8 + KP * 4 + KP * 4 + KP + 16;
+    return b;
 }
 
-__device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP) {
+__device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP, bool cache) {
     WarpShared w;
     unsigned char *p = base;
     w.tile = reinterpret_cast<float *>(p);
@@ -122,6 +167,14 @@ __device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP)
     w.flag = p; p += KP;
     p = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
     w.bar = reinterpret_cast<uint64_t *>(p);
+    p += 16;
+    w.centry = nullptr; w.cbound = nullptr; w.cflag = nullptr; w.vsh = nullptr;
+    if (cache) {
+        w.centry = reinterpret_cast<float2 *>(p); p += (size_t)KP * kCache * 8;
+        w.cbound = reinterpret_cast<float *>(p); p += KP * 4;
+        w.vsh = reinterpret_cast<float *>(p); p += KP * 4;
+        w.cflag = p;
+    }
     return w;
 }
 
@@ -202,6 +255,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
 
     float v[S], d[S], c[S];
     bool failed = false;
+    TMJV_T(t_col);
 
     // ---- column reduction (jonker_dense_flat.h:129-144) -------------------
     int ymin[S];
@@ -233,6 +287,8 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         }
     }
 
+    TMJV_ACC(1, t_col);
+    TMJV_T(t_claim);
     // ---- claim: highest column wins its row (:145-155) -------------------
 #pragma unroll
     for (int s = 0; s < S; ++s) {
@@ -255,6 +311,15 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     }
     __syncwarp();
 
+    // Row of each column in registers of its owner lane; prices of the
+    // padding lanes (column >= K) become -inf so their reduced costs are +inf.
+    int yc[S];
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+        yc[s] = (valid >> s & 1) ? (int)w.ycol[jj[s]] : -1;
+        if (!(valid >> s & 1)) v[s] = -__int_as_float(0x7f800000);
+    }
+
     // ---- free-row list and reduction transfer (:157-174) ------------------
     int nfree = 0;
     unsigned single_mask[S];
@@ -269,27 +334,20 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         if (isfree) w.queue[nfree + __popc(bf & ((1u << lane) - 1))] = (int16_t)r;
         nfree += __popc(bf);
     }
-    __syncwarp();
 #pragma unroll
     for (int s = 0; s < S; ++s) {
         unsigned m = single_mask[s];
         while (m) {
-            const int l = __ffs(m) - 1;
+            const int i = s * 32 + __ffs(m) - 1;
             m &= m - 1;
-            const int i = s * 32 + l;
             const int own = w.xrow[i];
             load_row<S, VEC, TILE>(src, i, N, M, lane, sanitize, sentinel, c);
             float loc = kBig;
 #pragma unroll
             for (int t = 0; t < S; ++t)
-                if ((valid >> t & 1) && jj[t] != own) loc = fminf(loc, c[t] - v[t]);
+                if (jj[t] != own) loc = fminf(loc, c[t] - v[t]);
             const float mn = warp_min_f(loc);
-            if (lane == L::lane_of(own)) {
-                const int so = L::slot_of(own);
-#pragma unroll
-                for (int t = 0; t < S; ++t)
-                    if (t == so) v[t] -= mn;
-            }
+            if (lane == L::lane_of(own)) setf(v, L::slot_of(own), sel(v, L::slot_of(own)) - mn);
         }
     }
     // flags now serve as per-column event bits; they start cleared
@@ -298,119 +356,195 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         const int r = s * 32 + lane;
         if (r < K) w.flag[r] = 0;
     }
-    __syncwarp();
+    TMJV_ACC(2, t_claim);
+    TMJV_T(t_arr);
 
     // ---- augmenting row reduction, at most two passes (:178-235) ----------
+    // In streaming mode every visited row keeps a cache of its kCache best
+    // columns and a lower bound on all the others.  Prices only fall during
+    // this phase, so reduced costs only rise; while the second-best cached
+    // value stays below the bound, the cached columns hold the exact
+    // lexicographic top-2 of the row and the row need not be read again.
+    constexpr bool kCached = !TILE;
+    const bool use_cache = kCached && K > kCache;
+    if (use_cache) {
+#pragma unroll
+        for (int s = 0; s < S; ++s) {
+            const int r = s * 32 + lane;
+            if (r < K) w.cflag[r] = 0;
+            if (valid >> s & 1) w.vsh[jj[s]] = v[s];
+        }
+    }
+    __syncwarp();
     for (int pass = 0; pass < 2 && nfree > 0 && !failed; ++pass) {
         unsigned head = 0, visits = 0;
         int kept = 0;
         const unsigned cap = (unsigned)K * (unsigned)K + 2u * K + 8u;
+        int row = w.queue[0];
         while (head < (unsigned)nfree) {
             if (++visits > cap) { failed = true; break; }
-            const int row = w.queue[head];
             ++head;
-            load_row<S, VEC, TILE>(src, row, N, M, lane, sanitize, sentinel, c);
-            float r[S];
-            float loc = __int_as_float(0x7f800000);
-            bool big = false;
+            // the next queued row; push-backs only write consumed slots
+            const int queued = w.queue[head < (unsigned)nfree ? head : 0];
+            float v1, v2, bv;
+            int j1, bc;
+            bool hit = false;
+            if (use_cache && w.cflag[row]) {
+                float cv = __int_as_float(0x7f800000);
+                int cj = 0x7fffffff;
+                if (lane < kCache) {
+                    const float2 e = w.centry[row * kCache + lane];
+                    cj = __float_as_int(e.y);
+                    cv = e.x - w.vsh[cj];
+                }
+                v1 = warp_min_f(cv);
+                j1 = (int)warp_min_u(cv == v1 ? (unsigned)cj : 0xffffffffu);
+                bv = cj == j1 ? __int_as_float(0x7f800000) : cv;
+                bc = cj;
+                v2 = warp_min_f(bv);
+                hit = v2 < w.cbound[row] && v2 < kBig;
+            }
+            if (!hit) {
+                load_row<S, VEC, TILE>(src, row, N, M, lane, sanitize, sentinel, c);
+                if (use_cache) {
+                    // lexicographic top-(kCache+1) by repeated extraction:
+                    // ranks 0-1 answer this step, ranks 0..kCache-1 are
+                    // cached, rank kCache bounds every uncached column
+                    unsigned gone = 0;
+                    float rk[kCache + 1];
+                    int jk[kCache + 1];
 #pragma unroll
-            for (int s = 0; s < S; ++s) {
-                r[s] = c[s] - v[s];
-                if (valid >> s & 1) {
-                    loc = fminf(loc, r[s]);
-                    big |= !(r[s] < kBig);
+                    for (int k = 0; k <= kCache; ++k) {
+                        float a = __int_as_float(0x7f800000);
+                        int sa = -1;
+#pragma unroll
+                        for (int t = 0; t < S; ++t) {
+                            const float x = c[t] - v[t];
+                            if (!(gone >> t & 1) && (valid >> t & 1) && (sa < 0 || x < a)) {
+                                a = x;
+                                sa = t;
+                            }
+                        }
+                        const int ja = sa >= 0 ? L::col(sa, lane) : 0x7fffffff;
+                        const float m = warp_min_f(a);
+                        const int jm = (int)warp_min_u(sa >= 0 && a == m ? (unsigned)ja
+                                                                         : 0xffffffffu);
+                        if (ja == jm) {
+                            gone |= 1u << sa;
+                            if (k < kCache)
+                                w.centry[row * kCache + k] =
+                                    make_float2(sel(c, sa), __int_as_float(jm));
+                        }
+                        rk[k] = m;
+                        jk[k] = jm;
+                    }
+                    if (lane == 0) {
+                        w.cbound[row] = rk[kCache];
+                        w.cflag[row] = 1;
+                    }
+                    v1 = rk[0];
+                    j1 = jk[0];
+                    v2 = rk[1];
+                    bv = v2;  // the lazy j2 lookup below then yields rank 1
+                    bc = jk[1];
+                } else {
+                    // lane-local lexicographic (value, column) top-2; the
+                    // slots of a lane ascend in column
+                    float a1 = c[0] - v[0], a2 = __int_as_float(0x7f800000);
+                    int c1 = jj[0], c2 = 0x7fffffff;
+#pragma unroll
+                    for (int t = 1; t < S; ++t) {
+                        const float x = c[t] - v[t];
+                        if (x < a1) { a2 = a1; c2 = c1; a1 = x; c1 = jj[t]; }
+                        else if (x < a2) { a2 = x; c2 = jj[t]; }
+                    }
+                    v1 = warp_min_f(a1);
+                    j1 = (int)warp_min_u(a1 == v1 ? (unsigned)c1 : 0xffffffffu);
+                    const bool mine = c1 == j1;
+                    bv = mine ? a2 : a1;
+                    bc = mine ? c2 : c1;
+                    v2 = warp_min_f(bv);
                 }
             }
-            int j1, j2;
-            float v1, v2;
-            if (!__any_sync(kFull, big)) {
-                // all reduced costs below LARGE: the reference's two-min scan
-                // is the lexicographic (value, column) top-2
-                v1 = warp_min_f(loc);
-                unsigned cand = 0xffffffffu;
+            int j2 = -2;  // -2: not computed yet
+            if (!(v2 < kBig)) {
+                // a reduced cost at or above LARGE: replay the scalar scan
+                // of :193-210 exactly (its result is not the plain top-2 then)
 #pragma unroll
-                for (int s = 0; s < S; ++s)
-                    if ((valid >> s & 1) && r[s] == v1) cand = min(cand, (unsigned)jj[s]);
-                j1 = (int)warp_min_u(cand);
-                float loc2 = __int_as_float(0x7f800000);
-#pragma unroll
-                for (int s = 0; s < S; ++s)
-                    if ((valid >> s & 1) && jj[s] != j1) loc2 = fminf(loc2, r[s]);
-                if (K > 1) {
-                    v2 = warp_min_f(loc2);
-                    unsigned cand2 = 0xffffffffu;
-#pragma unroll
-                    for (int s = 0; s < S; ++s)
-                        if ((valid >> s & 1) && jj[s] != j1 && r[s] == v2)
-                            cand2 = min(cand2, (unsigned)jj[s]);
-                    j2 = (int)warp_min_u(cand2);
-                } else {
-                    v2 = kBig;
-                    j2 = -1;
-                }
-            } else {
-                // rare: costs near LARGE -- replay the scalar scan exactly
-#pragma unroll
-                for (int s = 0; s < S; ++s)
-                    if (valid >> s & 1) w.dist[jj[s]] = r[s];
+                for (int t = 0; t < S; ++t)
+                    if (valid >> t & 1) w.dist[jj[t]] = c[t] - v[t];
                 __syncwarp();
-                int a = 0, bb = -1;
+                int ja = 0, jb = -1;
                 float va = 0.0f, vb = kBig;
                 if (lane == 0) {
                     va = w.dist[0];
                     for (int j = 1; j < K; ++j) {
                         const float t = w.dist[j];
                         if (t < vb) {
-                            if (t >= va) { vb = t; bb = j; }
-                            else { vb = va; bb = a; va = t; a = j; }
+                            if (t >= va) { vb = t; jb = j; }
+                            else { vb = va; jb = ja; va = t; ja = j; }
                         }
                     }
                 }
-                j1 = __shfl_sync(kFull, a, 0);
-                j2 = __shfl_sync(kFull, bb, 0);
+                j1 = __shfl_sync(kFull, ja, 0);
+                j2 = __shfl_sync(kFull, jb, 0);
                 v1 = __shfl_sync(kFull, va, 0);
                 v2 = __shfl_sync(kFull, vb, 0);
                 __syncwarp();
             }
-            int i0 = w.ycol[j1];
-            const float vj1 = __shfl_sync(kFull, sel(v, L::slot_of(j1)), L::lane_of(j1));
+            const int l1 = L::lane_of(j1), s1 = L::slot_of(j1);
+            const float vj1 = __shfl_sync(kFull, sel(v, s1), l1);
+            int i0 = __shfl_sync(kFull, seli(yc, s1), l1);
             const float lowered = vj1 - (v2 - v1);
             const bool lowers = lowered < vj1;
             int jsel = j1;
-            int push_front = -1, push_back = -1;
+            bool push_front = false, push_back = false;
             if (visits < head * (unsigned)K) {
                 if (lowers) {
-                    if (lane == L::lane_of(j1)) {
-                        const int so = L::slot_of(j1);
-#pragma unroll
-                        for (int t = 0; t < S; ++t)
-                            if (t == so) v[t] = lowered;
+                    if (lane == l1) {
+                        setf(v, s1, lowered);
+                        if (use_cache) w.vsh[j1] = lowered;
                     }
-                } else if (i0 >= 0 && j2 >= 0) {
-                    jsel = j2;
-                    i0 = w.ycol[j2];
+                } else if (i0 >= 0) {
+                    if (j2 == -2)
+                        j2 = (int)warp_min_u(bv == v2 ? (unsigned)bc : 0xffffffffu);
+                    if (j2 >= 0) {
+                        jsel = j2;
+                        i0 = __shfl_sync(kFull, seli(yc, L::slot_of(j2)), L::lane_of(j2));
+                    }
                 }
                 if (i0 >= 0) {
-                    if (lowers) push_front = i0;
-                    else push_back = i0;
+                    push_front = lowers;
+                    push_back = !lowers;
                 }
             } else if (i0 >= 0) {
-                push_back = i0;
+                push_back = true;
             }
-            __syncwarp();
-            if (push_front >= 0) --head;
+            if (lane == L::lane_of(jsel)) seti(yc, L::slot_of(jsel), row);
             if (lane == 0) {
-                if (push_front >= 0) w.queue[head] = (int16_t)push_front;
-                if (push_back >= 0) w.queue[kept] = (int16_t)push_back;
                 w.xrow[row] = jsel;
-                w.ycol[jsel] = (int16_t)row;
+                if (push_back) w.queue[kept] = (int16_t)i0;
             }
-            if (push_back >= 0) ++kept;
-            __syncwarp();
+            if (push_back) ++kept;
+            if (push_front) {
+                --head;
+                row = i0;
+            } else {
+                row = queued;
+            }
+            if (use_cache) __syncwarp();  // cache / price mirror writes visible
         }
         nfree = kept;
+        __syncwarp();
     }
+    // the Dijkstra phase reads y through shared memory
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+        if (valid >> s & 1) w.ycol[jj[s]] = (int16_t)yc[s];
+    __syncwarp();
 
+    TMJV_ACC(3, t_arr);
+    TMJV_T(t_sp);
     // ---- shortest augmenting paths (:75-122, :237-258) -------------------
     for (int f = 0; f < nfree && !failed; ++f) {
         const int start = w.queue[f];
@@ -605,6 +739,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         __syncwarp();
     }
 
+    TMJV_ACC(4, t_sp);
     // ---- output (cpu/ops.cpp:274-283) ------------------------------------
     int64_t *ob = P.out + b * (int64_t)N;
     for (int r = lane; r < N; r += 32) {
@@ -659,7 +794,8 @@ __global__ void __launch_bounds__(512) jv_batch_kernel(const Params P) {
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int wpb = blockDim.x >> 5;
-    WarpShared w = carve(smem_raw + (size_t)warp * P.warp_bytes, TILE ? P.tile_floats : 0, 32 * S);
+    WarpShared w = carve(smem_raw + (size_t)warp * P.warp_bytes, TILE ? P.tile_floats : 0, 32 * S,
+                         !TILE);
     const int64_t per = (int64_t)P.N * P.M;
     const uint32_t tile_bytes = (uint32_t)(per * 4);
     uint32_t phase = 0;
@@ -671,6 +807,7 @@ __global__ void __launch_bounds__(512) jv_batch_kernel(const Params P) {
     for (int64_t b = (int64_t)blockIdx.x * wpb + warp; b < P.B; b += stride) {
         const float *g = P.costs + b * per;
         const float *src = g;
+        TMJV_T(t_load);
         if constexpr (TILE) {
             bool ok = true;
             if (P.bulk_ok) {
@@ -693,6 +830,7 @@ __global__ void __launch_bounds__(512) jv_batch_kernel(const Params P) {
             const int64_t nb = b + stride;
             if (P.bulk_ok && lane == 0 && nb < P.B) prefetch_l2(P.costs + nb * per, tile_bytes);
         }
+        TMJV_ACC(0, t_load);
         solve_problem<S, VEC, TILE>(src, P, w, lane, b);
     }
 }
@@ -807,7 +945,7 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     const int KP = 32 * S;
     int tile_floats = 0;
     if (TILE) tile_floats = (int)(((int64_t)P.N * P.M + 31) / 32 * 32);
-    int warp_bytes = tile_floats * 4 + book_bytes(KP);
+    int warp_bytes = tile_floats * 4 + book_bytes(KP, !TILE);
     warp_bytes = (warp_bytes + 127) & ~127;
     P.warp_bytes = warp_bytes;
     P.tile_floats = tile_floats;
@@ -841,7 +979,7 @@ static int launch(Params P, cudaStream_t stream) {
     P.bulk_ok = ((base & 15) == 0) && ((per * 4) % 16 == 0);
     // TILE mode while at least tile_min_warps() warps fit on one SM with
     // their tiles; larger matrices stream their rows from L2/HBM.
-    const int64_t tile_bytes = ((per + 31) / 32 * 32) * 4 + book_bytes(32 * S);
+    const int64_t tile_bytes = ((per + 31) / 32 * 32) * 4 + book_bytes(32 * S, false);
     const bool tile = tile_bytes * tile_min_warps() <= kSmemLimit;
     const bool v4 = (P.M % 4 == 0) && (base % 16 == 0);
     const bool v2 = (P.M % 2 == 0) && (base % 8 == 0);
@@ -975,3 +1113,14 @@ int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64
 }
 
 }  // extern "C"
+
+#ifdef TMJV_PHASE_CLOCKS
+// Reads and clears the per-phase cycle counters (debug builds only).
+extern "C" int tm_phase_read(unsigned long long *host8) {
+    cudaDeviceSynchronize();
+    cudaMemcpyFromSymbol(host8, tmjv::tmjv_phase_cycles, sizeof(unsigned long long) * 8);
+    unsigned long long z[8] = {0};
+    cudaMemcpyToSymbol(tmjv::tmjv_phase_cycles, z, sizeof(z));
+    return 0;
+}
+#endif
