@@ -307,12 +307,12 @@ def run_ours(args):
     value = b * world * args.steps / (ms / 1e3)
 
     # ---- kernel-only timing of the solve launch (roofline) ----------------
-    stats = torch.empty(2, dtype=torch.int32, device=dev)
+    stats = torch.empty(lib.tm_jv_workspace_bytes() // 4, dtype=torch.int32, device=dev)
     x0 = bufs[0]
     out = torch.empty(b, n, dtype=torch.long, device=dev)
     stream = torch.cuda.current_stream().cuda_stream
     lib.tm_jv_stats_f32(x0.data_ptr(), x0.numel(), stats.data_ptr(), stream)
-    flags, key = (int(v) & 0xFFFFFFFF for v in stats.cpu().tolist())
+    flags, key = (int(v) & 0xFFFFFFFF for v in stats[:2].cpu().tolist())
     sentinel, pinf = sharded.sentinel_from_words(sharded.stats_words(flags, key), max(n, m))
     reps = max(3, min(args.steps, 50))
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -326,7 +326,7 @@ def run_ours(args):
         sevs[r][1].record()
         evs[r][0].record()
         rc = lib.tm_jv_solve_f32(x.data_ptr(), b, n, m, sentinel, int(pinf), out.data_ptr(),
-                                 None, stream)
+                                 stats.data_ptr(), stream)
         evs[r][1].record()
         assert rc == 0, lib.tm_status_string(rc)
     torch.cuda.synchronize()

@@ -55,6 +55,17 @@ typedef struct tm_jv_stats {
     uint32_t max_key;   /* order-preserving key of the largest finite cell   */
 } tm_jv_stats;
 
+/* Device scratch of one solve (tm_jv_workspace_bytes() bytes).  `ticket`
+ * hands out problems to warps; tm_jv_solve_f32 zeroes it and `status` on
+ * the stream before each launch.  `status` receives TM_ERR_UNSOLVED (bit
+ * OR) if a problem hit a loop bound; that problem's row is all -1. */
+typedef struct tm_jv_workspace {
+    tm_jv_stats stats;
+    unsigned long long ticket;
+    int32_t status;
+    int32_t reserved[11];
+} tm_jv_workspace;
+
 #define TM_STAT_NAN      1u
 #define TM_STAT_NEG_INF  2u
 #define TM_STAT_FINITE   4u
@@ -78,15 +89,16 @@ int tm_jv_sentinel(const tm_jv_stats *stats_host, int K, float *sentinel,
 
 /* Solves B problems of shape (N, M), costs contiguous fp32 (B, N, M),
  * into out (B, N) int64 (row -> column, -1 = unmatched).  `sentinel`
- * replaces +inf cells (only read when has_pos_inf != 0).  `status_dev`
- * (may be NULL) is a device int32 that receives TM_ERR_UNSOLVED via
- * atomicOr if any problem hits a loop bound; the caller zeroes it.
+ * replaces +inf cells (only read when has_pos_inf != 0).  `workspace` is
+ * device memory of tm_jv_workspace_bytes() (a tm_jv_workspace) that this
+ * call re-initialises on the stream; concurrent solves need their own.
  * Replaces cuda/cuda_common.cuh:270-284 + cuda/jonker_tiled.cuh:203-218. */
 int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
-                    int has_pos_inf, int64_t *out, int32_t *status_dev,
+                    int has_pos_inf, int64_t *out, void *workspace,
                     tm_stream_t stream);
 
-/* Device scratch needed by tm_jonker_dense_batch_f32 (bytes). */
+/* Bytes of device scratch (a tm_jv_workspace) for tm_jv_solve_f32 and
+ * tm_jonker_dense_batch_f32. */
 size_t tm_jv_workspace_bytes(void);
 
 /* The whole jonker_dense_batch op for a caller without torch: statistics,

@@ -85,6 +85,9 @@ def test_solve_argument_checks_need_no_gpu():
     lib = _core()
     assert lib.tm_jv_solve_f32(None, -1, 2, 2, 1.0, 0, None, None, None) == 3
     assert lib.tm_jv_solve_f32(None, 0, 2, 2, 1.0, 0, None, None, None) == 0
+    assert lib.tm_jv_solve_f32(ctypes.c_void_p(16), 1, 2, 2, 1.0, 0, ctypes.c_void_p(16),
+                               None, None) == 3  # no workspace
     assert lib.tm_jv_solve_f32(ctypes.c_void_p(16), 1, 257, 3, 1.0, 0, ctypes.c_void_p(16),
-                               None, None) == 5
+                               ctypes.c_void_p(64), None) == 5
+    assert lib.tm_jv_workspace_bytes() == 64
     assert lib.tm_jonker_dense_batch_f32(None, 2, 3, 3, None, None, None) == 3

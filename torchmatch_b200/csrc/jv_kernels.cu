@@ -64,6 +64,7 @@ struct Params {
     int sanitize;        // batch holds +inf cells
     int64_t *out;
     int32_t *status;
+    unsigned long long *ticket;  // next unclaimed problem (zeroed per launch)
     int warp_bytes;      // shared-memory bytes per warp
     int tile_floats;     // floats reserved for the staged tile (TILE mode)
     int bulk_ok;         // tile base and size are 16-byte multiples
@@ -86,9 +87,12 @@ struct Layout {
     __device__ static __forceinline__ int col(int s, int lane) {
         return (s / VEC) * (32 * VEC) + lane * VEC + (s % VEC);
     }
-    __device__ static __forceinline__ int lane_of(int j) { return (j % (32 * VEC)) / VEC; }
+    // columns are never negative here: unsigned math keeps these to shifts
+    __device__ static __forceinline__ int lane_of(int j) {
+        return (int)(((unsigned)j % (32u * VEC)) / VEC);
+    }
     __device__ static __forceinline__ int slot_of(int j) {
-        return (j / (32 * VEC)) * VEC + (j % VEC);
+        return (int)(((unsigned)j / (32u * VEC)) * VEC + ((unsigned)j % VEC));
     }
 };
 
@@ -183,11 +187,39 @@ __device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP,
 // stride M), zeros in the padding (cpu/ops.cpp:262-270).  In streaming mode
 // +inf cells become the sentinel here; in TILE mode the tile was already
 // sanitised.
-template <int S, int VEC, bool TILE>
+template <int S, int VEC, bool TILE, bool FULL>
 __device__ __forceinline__ void load_row(const float *__restrict__ src, int i, int N, int M,
                                          int lane, bool sanitize, float sentinel,
                                          float (&c)[S]) {
     using L = Layout<S, VEC>;
+    if constexpr (FULL) {
+        // square, no padding, K a multiple of 32 * VEC: one aligned vector
+        // load per group and no bounds checks
+        const float *row = src + i * (32 * S) + lane * VEC;
+#pragma unroll
+        for (int g = 0; g < S / VEC; ++g) {
+            const float *q = row + g * 32 * VEC;
+            if constexpr (VEC == 4) {
+                const float4 t = TILE ? *reinterpret_cast<const float4 *>(q)
+                                      : __ldg(reinterpret_cast<const float4 *>(q));
+                c[g * 4 + 0] = t.x; c[g * 4 + 1] = t.y; c[g * 4 + 2] = t.z; c[g * 4 + 3] = t.w;
+            } else if constexpr (VEC == 2) {
+                const float2 t = TILE ? *reinterpret_cast<const float2 *>(q)
+                                      : __ldg(reinterpret_cast<const float2 *>(q));
+                c[g * 2 + 0] = t.x; c[g * 2 + 1] = t.y;
+            } else {
+                c[g] = TILE ? *q : __ldg(q);
+            }
+        }
+        if constexpr (!TILE) {
+            if (sanitize) {
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if (isinf(c[s])) c[s] = sentinel;
+            }
+        }
+        return;
+    }
     if (i >= N) {
 #pragma unroll
         for (int s = 0; s < S; ++s) c[s] = 0.0f;
@@ -235,11 +267,14 @@ __device__ __forceinline__ void load_row(const float *__restrict__ src, int i, i
 }
 
 // ------------------------------------------------------------- one solve
-template <int S, int VEC, bool TILE>
+template <int S, int VEC, bool TILE, bool FULL>
 __device__ void solve_problem(const float *__restrict__ src, const Params &P, WarpShared &w,
                               int lane, int64_t b) {
     using L = Layout<S, VEC>;
-    const int K = P.K, N = P.N, M = P.M;
+    // FULL: N == M == K == 32 * S, known at compile time
+    const int K = FULL ? 32 * S : P.K;
+    const int N = FULL ? 32 * S : P.N;
+    const int M = FULL ? 32 * S : P.M;
     const bool sanitize = P.sanitize != 0;
     const float sentinel = P.sentinel;
     constexpr int KP = 32 * S;
@@ -252,6 +287,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         jj[s] = L::col(s, lane);
         if (jj[s] < K) valid |= 1u << s;
     }
+    if constexpr (FULL) valid = (1u << S) - 1;
 
     float v[S], d[S], c[S];
     bool failed = false;
@@ -266,8 +302,8 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         int i = 0;
         for (; i + 2 <= nreal; i += 2) {
             float c0[S], c1[S];
-            load_row<S, VEC, TILE>(src, i, N, M, lane, sanitize, sentinel, c0);
-            load_row<S, VEC, TILE>(src, i + 1, N, M, lane, sanitize, sentinel, c1);
+            load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c0);
+            load_row<S, VEC, TILE, FULL>(src, i + 1, N, M, lane, sanitize, sentinel, c1);
 #pragma unroll
             for (int s = 0; s < S; ++s) {
                 if (c0[s] < v[s]) { v[s] = c0[s]; ymin[s] = i; }
@@ -275,7 +311,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             }
         }
         for (; i < nreal; ++i) {
-            load_row<S, VEC, TILE>(src, i, N, M, lane, sanitize, sentinel, c);
+            load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c);
 #pragma unroll
             for (int s = 0; s < S; ++s)
                 if (c[s] < v[s]) { v[s] = c[s]; ymin[s] = i; }
@@ -341,7 +377,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             const int i = s * 32 + __ffs(m) - 1;
             m &= m - 1;
             const int own = w.xrow[i];
-            load_row<S, VEC, TILE>(src, i, N, M, lane, sanitize, sentinel, c);
+            load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c);
             float loc = kBig;
 #pragma unroll
             for (int t = 0; t < S; ++t)
@@ -405,7 +441,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 hit = v2 < w.cbound[row] && v2 < kBig;
             }
             if (!hit) {
-                load_row<S, VEC, TILE>(src, row, N, M, lane, sanitize, sentinel, c);
+                load_row<S, VEC, TILE, FULL>(src, row, N, M, lane, sanitize, sentinel, c);
                 if (use_cache) {
                     // lexicographic top-(kCache+1) by repeated extraction:
                     // ranks 0-1 answer this step, ranks 0..kCache-1 are
@@ -548,7 +584,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     // ---- shortest augmenting paths (:75-122, :237-258) -------------------
     for (int f = 0; f < nfree && !failed; ++f) {
         const int start = w.queue[f];
-        load_row<S, VEC, TILE>(src, start, N, M, lane, sanitize, sentinel, c);
+        load_row<S, VEC, TILE, FULL>(src, start, N, M, lane, sanitize, sentinel, c);
         unsigned todo = valid, ready = 0, grp = 0;
 #pragma unroll
         for (int s = 0; s < S; ++s) {
@@ -650,7 +686,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 const float dj = w.dist[j];
                 const int lj = L::lane_of(j), sj = L::slot_of(j);
                 const float vj = __shfl_sync(kFull, sel(v, sj), lj);
-                load_row<S, VEC, TILE>(src, i, N, M, lane, sanitize, sentinel, c);
+                load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c);
                 const float cij = __shfl_sync(kFull, sel(c, sj), lj);
                 const float h = cij - vj - dj;
                 unsigned ev = 0;
@@ -788,8 +824,8 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
 }
 
 // ------------------------------------------------------------------ kernel
-template <int S, int VEC, bool TILE>
-__global__ void __launch_bounds__(512) jv_batch_kernel(const Params P) {
+template <int S, int VEC, bool TILE, bool FULL>
+__global__ void __launch_bounds__(512, 1) jv_batch_kernel(const Params P) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -803,8 +839,18 @@ __global__ void __launch_bounds__(512) jv_batch_kernel(const Params P) {
         if (lane == 0) bar_init(w.bar);
         __syncwarp();
     }
-    const int64_t stride = (int64_t)gridDim.x * wpb;
-    for (int64_t b = (int64_t)blockIdx.x * wpb + warp; b < P.B; b += stride) {
+    // Problems are claimed one at a time from a global ticket: the work per
+    // problem is heavy-tailed, so a static split would leave warps idle
+    // behind the unlucky ones.  The next ticket is taken before solving the
+    // current problem so its tile can be prefetched into L2 meanwhile.
+    auto claim = [&]() -> int64_t {
+        unsigned long long t = 0;
+        if (lane == 0) t = atomicAdd(P.ticket, 1ull);
+        return (int64_t)__shfl_sync(kFull, t, 0);
+    };
+    int64_t b = claim();
+    while (b < P.B) {
+        const int64_t nb = claim();
         const float *g = P.costs + b * per;
         const float *src = g;
         TMJV_T(t_load);
@@ -827,11 +873,11 @@ __global__ void __launch_bounds__(512) jv_batch_kernel(const Params P) {
             }
             __syncwarp();
             src = w.tile;
-            const int64_t nb = b + stride;
             if (P.bulk_ok && lane == 0 && nb < P.B) prefetch_l2(P.costs + nb * per, tile_bytes);
         }
         TMJV_ACC(0, t_load);
-        solve_problem<S, VEC, TILE>(src, P, w, lane, b);
+        solve_problem<S, VEC, TILE, FULL>(src, P, w, lane, b);
+        b = nb;
     }
 }
 
@@ -939,7 +985,7 @@ static int tile_min_warps() {
 }
 constexpr int kMaxWarpsPerBlock = 16;
 
-template <int S, int VEC, bool TILE>
+template <int S, int VEC, bool TILE, bool FULL>
 static int launch_t(const Params &P0, cudaStream_t stream) {
     Params P = P0;
     const int KP = 32 * S;
@@ -955,7 +1001,7 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     const int64_t need_warps = P.B;
     if ((int64_t)wpb > need_warps) wpb = (int)need_warps;
     const int smem = wpb * warp_bytes;
-    auto kern = jv_batch_kernel<S, VEC, TILE>;
+    auto kern = jv_batch_kernel<S, VEC, TILE, FULL>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return cuda_fail(e);
     int per_sm = 0;
@@ -983,20 +1029,27 @@ static int launch(Params P, cudaStream_t stream) {
     const bool tile = tile_bytes * tile_min_warps() <= kSmemLimit;
     const bool v4 = (P.M % 4 == 0) && (base % 16 == 0);
     const bool v2 = (P.M % 2 == 0) && (base % 8 == 0);
-#define TM_L(SS, VV)                                                        \
-    return tile ? launch_t<SS, VV, true>(P, stream) : launch_t<SS, VV, false>(P, stream)
+    // square problems with K a multiple of 32 take the padding-free path
+    const bool full = P.N == P.M && P.M == 32 * S;
+#define TM_L(SS, VV)                                                                     \
+    return tile ? launch_t<SS, VV, true, false>(P, stream)                               \
+                : launch_t<SS, VV, false, false>(P, stream)
+#define TM_F(SS, VV)                                                                     \
+    return tile ? launch_t<SS, VV, true, true>(P, stream)                                \
+                : launch_t<SS, VV, false, true>(P, stream)
     switch (S) {
-    case 1: TM_L(1, 1);
-    case 2: if (v2) { TM_L(2, 2); } TM_L(2, 1);
+    case 1: if (full) { TM_F(1, 1); } TM_L(1, 1);
+    case 2: if (full && v2) { TM_F(2, 2); } if (v2) { TM_L(2, 2); } TM_L(2, 1);
     case 3: TM_L(3, 1);
-    case 4: if (v4) { TM_L(4, 4); } TM_L(4, 1);
+    case 4: if (full && v4) { TM_F(4, 4); } if (v4) { TM_L(4, 4); } TM_L(4, 1);
     case 5: TM_L(5, 1);
     case 6: if (v2) { TM_L(6, 2); } TM_L(6, 1);
     case 7: TM_L(7, 1);
-    case 8: if (v4) { TM_L(8, 4); } TM_L(8, 1);
+    case 8: if (full && v4) { TM_F(8, 4); } if (v4) { TM_L(8, 4); } TM_L(8, 1);
     default: return TM_ERR_TOO_LARGE;
     }
 #undef TM_L
+#undef TM_F
 }
 
 }  // namespace tmjv
@@ -1058,11 +1111,11 @@ int tm_jv_sentinel(const tm_jv_stats *st, int K, float *sentinel, int *has_pos_i
 }
 
 int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
-                    int has_pos_inf, int64_t *out, int32_t *status_dev, tm_stream_t stream_) {
+                    int has_pos_inf, int64_t *out, void *workspace, tm_stream_t stream_) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
     if (B == 0 || N == 0) return TM_OK;
-    if (!out || (M > 0 && !costs)) return TM_ERR_ARG;
+    if (!out || !workspace || (M > 0 && !costs)) return TM_ERR_ARG;
     const int K = N > M ? N : M;
     if (K > 32 * tmjv::kMaxSlots) return TM_ERR_TOO_LARGE;
     tmjv::StreamDevice scope(stream);
@@ -1071,6 +1124,9 @@ int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
         cudaError_t e = cudaMemsetAsync(out, 0xff, sizeof(int64_t) * (size_t)B * N, stream);
         return e == cudaSuccess ? TM_OK : tmjv::cuda_fail(e);
     }
+    tm_jv_workspace *ws = reinterpret_cast<tm_jv_workspace *>(workspace);
+    cudaError_t e = cudaMemsetAsync(&ws->ticket, 0, sizeof(ws->ticket) + sizeof(ws->status), stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
     tmjv::Params P{};
     P.costs = costs;
     P.B = B;
@@ -1080,11 +1136,12 @@ int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
     P.sentinel = sentinel;
     P.sanitize = has_pos_inf ? 1 : 0;
     P.out = out;
-    P.status = status_dev;
+    P.status = &ws->status;
+    P.ticket = &ws->ticket;
     return tmjv::launch(P, stream);
 }
 
-size_t tm_jv_workspace_bytes(void) { return 256; }
+size_t tm_jv_workspace_bytes(void) { return sizeof(tm_jv_workspace); }
 
 int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64_t *out,
                               void *workspace, tm_stream_t stream_) {
@@ -1094,10 +1151,10 @@ int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64
     if (!out || !workspace) return TM_ERR_ARG;
     tmjv::StreamDevice scope(stream);
     if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
-    if (M == 0) return tm_jv_solve_f32(costs, B, N, M, 0.0f, 0, out, nullptr, stream_);
+    if (M == 0) return tm_jv_solve_f32(costs, B, N, M, 0.0f, 0, out, workspace, stream_);
     const int K = N > M ? N : M;
     if (K > tm_jv_max_k()) return TM_ERR_TOO_LARGE;
-    tm_jv_stats *st = reinterpret_cast<tm_jv_stats *>(workspace);
+    tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
     int rc = tm_jv_stats_f32(costs, B * (int64_t)N * M, st, stream_);
     if (rc) return rc;
     tm_jv_stats h{};
@@ -1109,7 +1166,7 @@ int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64
     int pinf = 0;
     rc = tm_jv_sentinel(&h, K, &sentinel, &pinf);
     if (rc) return rc;
-    return tm_jv_solve_f32(costs, B, N, M, sentinel, pinf, out, nullptr, stream_);
+    return tm_jv_solve_f32(costs, B, N, M, sentinel, pinf, out, workspace, stream_);
 }
 
 }  // extern "C"

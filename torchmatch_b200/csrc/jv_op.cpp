@@ -67,8 +67,11 @@ at::Tensor jonker_dense_batch_cuda(const at::Tensor &costs) {
     const float *cp = c.const_data_ptr<float>();
     auto stream_h = reinterpret_cast<tm_stream_t>(stream);
 
-    at::Tensor stats = at::empty({(int64_t)sizeof(tm_jv_stats)}, c.options().dtype(at::kByte));
-    auto *st_dev = reinterpret_cast<tm_jv_stats *>(stats.mutable_data_ptr());
+    // one small scratch block: batch statistics + the solve's work ticket
+    at::Tensor scratch =
+        at::empty({(int64_t)tm_jv_workspace_bytes()}, c.options().dtype(at::kByte));
+    auto *ws = reinterpret_cast<tm_jv_workspace *>(scratch.mutable_data_ptr());
+    auto *st_dev = &ws->stats;
     int rc = tm_jv_stats_f32(cp, c.numel(), st_dev, stream_h);
     TORCH_CHECK(rc == TM_OK, "batched JV statistics failed: ", status_text(rc));
     tm_jv_stats host{};
@@ -86,7 +89,7 @@ at::Tensor jonker_dense_batch_cuda(const at::Tensor &costs) {
 
     at::Tensor out = at::empty({B, N}, costs.options().dtype(at::kLong));
     rc = tm_jv_solve_f32(cp, B, static_cast<int>(N), static_cast<int>(M), sentinel, has_pos_inf,
-                         out.mutable_data_ptr<int64_t>(), nullptr, stream_h);
+                         out.mutable_data_ptr<int64_t>(), ws, stream_h);
     TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
     return out;
 }

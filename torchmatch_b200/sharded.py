@@ -74,11 +74,11 @@ def _stream(dev: torch.device) -> int:
 
 def _local_stats(c: torch.Tensor) -> list[int]:
     lib = _loader.core()
-    st = torch.empty(2, dtype=torch.int32, device=c.device)
+    st = torch.empty(lib.tm_jv_workspace_bytes() // 4, dtype=torch.int32, device=c.device)
     rc = lib.tm_jv_stats_f32(c.data_ptr(), c.numel(), st.data_ptr(), _stream(c.device))
     if rc != 0:
         raise RuntimeError("jonker_dense_batch statistics: " + lib.tm_status_string(rc).decode())
-    flags, key = (int(v) & 0xFFFFFFFF for v in st.cpu().tolist())
+    flags, key = (int(v) & 0xFFFFFFFF for v in st[:2].cpu().tolist())
     return stats_words(flags, key)
 
 
@@ -88,8 +88,9 @@ def _solve_local(c: torch.Tensor, sentinel: float, pinf: bool) -> torch.Tensor:
     out = torch.empty(b, n, dtype=torch.long, device=c.device)
     if b == 0 or n == 0:
         return out
-    rc = lib.tm_jv_solve_f32(c.data_ptr(), b, n, m, sentinel, int(pinf), out.data_ptr(), None,
-                             _stream(c.device))
+    ws = torch.empty(lib.tm_jv_workspace_bytes(), dtype=torch.uint8, device=c.device)
+    rc = lib.tm_jv_solve_f32(c.data_ptr(), b, n, m, sentinel, int(pinf), out.data_ptr(),
+                             ws.data_ptr(), _stream(c.device))
     if rc != 0:
         raise RuntimeError("batched JV kernel launch failed: " + lib.tm_status_string(rc).decode())
     return out
