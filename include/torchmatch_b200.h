@@ -108,6 +108,20 @@ size_t tm_jv_workspace_bytes(void);
 int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M,
                               int64_t *out, void *workspace, tm_stream_t stream);
 
+/* Same as tm_jonker_dense_batch_f32, for callers that may not allocate
+ * device memory themselves (no cudaMalloc and no caching allocator in their
+ * process, e.g. an embedding runtime that owns all GPU memory or a hook that
+ * runs where allocation is forbidden).  No counterpart in the reference.
+ * Its scratch is a fixed 64-byte array in this library's device memory, one
+ * per GPU, kept until the process exits, so the only size limit is the
+ * solver's own max(N, M) <= tm_jv_max_k() (TM_ERR_TOO_LARGE beyond it).
+ * The first call on a device looks up that array's device address; make it
+ * before any stream capture.  All calls on one device share the array:
+ * calls that overlap on the GPU (other streams, other host threads) race
+ * and must be serialised by the caller.  Nothing is allocated or freed. */
+int tm_jonker_dense_batch_f32_noalloc(const float *costs, int64_t B, int N, int M,
+                                      int64_t *out, tm_stream_t stream);
+
 /* The cudaError_t of the last TM_ERR_CUDA on this thread. */
 int tm_last_cuda_error(void);
 

@@ -1181,3 +1181,43 @@ extern "C" int tm_phase_read(unsigned long long *host8) {
     return 0;
 }
 #endif
+
+// ============================================= allocation-free entry point
+// Scratch of tm_jonker_dense_batch_f32_noalloc: one tm_jv_workspace (64
+// bytes) per GPU that loads this library, held until the process exits.
+// Host code must not pass `g_noalloc_workspace` itself to a kernel (on the
+// host it names a stand-in, not device memory); it asks the runtime for the
+// device address once per device.
+static __device__ __align__(256) tm_jv_workspace g_noalloc_workspace;
+
+#include <mutex>
+
+namespace {
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[64] = {nullptr};
+}  // namespace
+
+extern "C" int tm_jonker_dense_batch_f32_noalloc(const float *costs, int64_t B, int N, int M,
+                                                 int64_t *out, tm_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
+    if (B == 0 || N == 0) return TM_OK;
+    if (!out || (M > 0 && !costs)) return TM_ERR_ARG;
+    if ((N > M ? N : M) > tm_jv_max_k()) return TM_ERR_TOO_LARGE;
+    tmjv::StreamDevice scope(stream);  // the stream's device is current from here on
+    if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
+    if (scope.dev < 0 || scope.dev >= 64) return TM_ERR_ARG;
+    void *ws = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_ptr[scope.dev]) {
+            void *p = nullptr;
+            const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_workspace);
+            if (e != cudaSuccess) return tmjv::cuda_fail(e);
+            g_noalloc_ptr[scope.dev] = p;
+        }
+        ws = g_noalloc_ptr[scope.dev];
+    }
+    // the regular entry point zeroes the statistics and the work ticket
+    return tm_jonker_dense_batch_f32(costs, B, N, M, out, ws, stream_);
+}
