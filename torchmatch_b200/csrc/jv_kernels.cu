@@ -495,11 +495,17 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                         else if (x < a2) { a2 = x; c2 = jj[t]; }
                     }
                     v1 = warp_min_f(a1);
-                    j1 = (int)warp_min_u(a1 == v1 ? (unsigned)c1 : 0xffffffffu);
+                    const bool at1 = a1 == v1;
+                    const unsigned ties = __ballot_sync(kFull, at1);
+                    j1 = (int)warp_min_u(at1 ? (unsigned)c1 : 0xffffffffu);
+                    // the second best does not wait for j1: with two lanes at
+                    // v1 it is v1 itself, else the lane at v1 offers its own
+                    // second value
+                    const float v2b = warp_min_f(at1 ? a2 : a1);
+                    v2 = __popc(ties) > 1 ? v1 : v2b;
                     const bool mine = c1 == j1;
-                    bv = mine ? a2 : a1;
+                    bv = mine ? a2 : a1;  // only read by the rare j2 lookup
                     bc = mine ? c2 : c1;
-                    v2 = warp_min_f(bv);
                 }
             }
             int j2 = -2;  // -2: not computed yet
@@ -534,40 +540,40 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             const float lowered = vj1 - (v2 - v1);
             const bool lowers = lowered < vj1;
             int jsel = j1;
+            const bool early = visits < head * (unsigned)K;  // rr_cnt < current * n
             bool push_front = false, push_back = false;
-            if (visits < head * (unsigned)K) {
-                if (lowers) {
-                    if (lane == l1) {
-                        setf(v, s1, lowered);
-                        if (use_cache) w.vsh[j1] = lowered;
-                    }
-                } else if (i0 >= 0) {
-                    if (j2 == -2)
-                        j2 = (int)warp_min_u(bv == v2 ? (unsigned)bc : 0xffffffffu);
-                    if (j2 >= 0) {
-                        jsel = j2;
-                        i0 = __shfl_sync(kFull, seli(yc, L::slot_of(j2)), L::lane_of(j2));
-                    }
+            if (early && !lowers && i0 >= 0) {
+                if (j2 == -2) j2 = (int)warp_min_u(bv == v2 ? (unsigned)bc : 0xffffffffu);
+                if (j2 >= 0) {
+                    jsel = j2;
+                    i0 = __shfl_sync(kFull, seli(yc, L::slot_of(j2)), L::lane_of(j2));
                 }
-                if (i0 >= 0) {
-                    push_front = lowers;
-                    push_back = !lowers;
-                }
-            } else if (i0 >= 0) {
-                push_back = true;
             }
-            if (lane == L::lane_of(jsel)) seti(yc, L::slot_of(jsel), row);
+            if (i0 >= 0) {
+                push_front = early && lowers;
+                push_back = !push_front;
+            }
+            // branch-free register updates of the owner lanes
+            const bool own1 = early && lowers && lane == l1;
+            const int ls = L::lane_of(jsel), ss = L::slot_of(jsel);
+            if constexpr (S <= 2) {
+#pragma unroll
+                for (int t = 0; t < S; ++t) {
+                    v[t] = (own1 && t == s1) ? lowered : v[t];
+                    yc[t] = (lane == ls && t == ss) ? row : yc[t];
+                }
+            } else {
+                if (own1) setf(v, s1, lowered);
+                if (lane == ls) seti(yc, ss, row);
+            }
+            if (use_cache && own1) w.vsh[j1] = lowered;
             if (lane == 0) {
                 w.xrow[row] = jsel;
                 if (push_back) w.queue[kept] = (int16_t)i0;
             }
-            if (push_back) ++kept;
-            if (push_front) {
-                --head;
-                row = i0;
-            } else {
-                row = queued;
-            }
+            kept += push_back;
+            head -= push_front;
+            row = push_front ? i0 : queued;
             if (use_cache) __syncwarp();  // cache / price mirror writes visible
         }
         nfree = kept;
@@ -825,7 +831,7 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
 
 // ------------------------------------------------------------------ kernel
 template <int S, int VEC, bool TILE, bool FULL>
-__global__ void __launch_bounds__(512, 1) jv_batch_kernel(const Params P) {
+__global__ void __launch_bounds__(TILE ? 512 : 256, TILE ? 1 : (S > 4 ? 2 : 4)) jv_batch_kernel(const Params P) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -996,7 +1002,7 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     P.warp_bytes = warp_bytes;
     P.tile_floats = tile_floats;
     int wpb = kSmemLimit / warp_bytes;
-    if (wpb > kMaxWarpsPerBlock) wpb = kMaxWarpsPerBlock;
+    if (wpb > (TILE ? kMaxWarpsPerBlock : 8)) wpb = TILE ? kMaxWarpsPerBlock : 8;
     if (wpb < 1) return TM_ERR_TOO_LARGE;
     const int64_t need_warps = P.B;
     if ((int64_t)wpb > need_warps) wpb = (int)need_warps;

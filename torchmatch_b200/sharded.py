@@ -96,14 +96,24 @@ def _solve_local(c: torch.Tensor, sentinel: float, pinf: bool) -> torch.Tensor:
     return out
 
 
+def merge_words(words: list[int], group=None, device=None) -> list[int]:
+    """The one exchange of a sharded solve: element-wise MAX of every rank's
+    five statistics words (flags are 0/1, the key is order-preserving, so
+    MAX is OR of the flags and max of the largest finite cell)."""
+    import torch.distributed as dist
+
+    dev = device if dist.get_backend(group) == "nccl" else torch.device("cpu")
+    t = torch.tensor(words, dtype=torch.int64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return t.cpu().tolist()
+
+
 def solve_sharded(local: torch.Tensor, group=None) -> torch.Tensor:
     """Solve this rank's contiguous slice (B_r, N, M) of one global batch.
 
     Collective over ``group`` (every rank calls it with the same N, M).
     Returns the (B_r, N) int64 mapping of the local slice.
     """
-    import torch.distributed as dist
-
     if local.dim() != 3:
         raise RuntimeError("costs must be 3D (B, N, M)")
     c = local.to(torch.float32).contiguous()
@@ -111,11 +121,7 @@ def solve_sharded(local: torch.Tensor, group=None) -> torch.Tensor:
     if k > _loader.core().tm_jv_max_k():
         raise RuntimeError(f"Batched JV (CUDA) supports max(N, M) <= 256, got K={k}")
     words = _local_stats(c) if c.numel() else [0, 0, 0, 0, 0]
-    backend = dist.get_backend(group)
-    dev = c.device if backend == "nccl" else torch.device("cpu")
-    t = torch.tensor(words, dtype=torch.int64, device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
-    sentinel, pinf = sentinel_from_words(t.cpu().tolist(), k)
+    sentinel, pinf = sentinel_from_words(merge_words(words, group, c.device), k)
     if c.size(2) == 0:
         return torch.full((c.size(0), c.size(1)), -1, dtype=torch.long, device=c.device)
     return _solve_local(c, sentinel, pinf)
