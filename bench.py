@@ -280,12 +280,21 @@ def run_ours(args):
     for k in range(args.warmup):
         step(bufs[k % nbuf])
     barrier()
+    # Keep the GPU loaded for ~0.5 s on both sides of the timed region so the
+    # clock sampler sees it under load.  Every rank runs the same number of
+    # steps (each step of a sharded solve is a collective).
+    tw = time.perf_counter()
+    step(bufs[0])
+    barrier()
+    per = torch.tensor([time.perf_counter() - tw], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(per, op=dist.ReduceOp.MAX)
+    n_load = max(1, min(2000, int(0.5 / max(float(per.item()), 1e-6))))
     if clocks:
         clocks.start()
-        t_load = time.perf_counter() + 0.5
-        while time.perf_counter() < t_load:  # let the sampler see the GPU under load
-            step(bufs[0])
-        barrier()
+    for _ in range(n_load):
+        step(bufs[0])
+    barrier()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record()
@@ -294,11 +303,10 @@ def run_ours(args):
     t1.record()
     barrier()
     ms = t0.elapsed_time(t1)
+    for _ in range(max(1, n_load // 2)):
+        step(bufs[0])
+    barrier()
     if clocks:
-        t_load = time.perf_counter() + 0.3
-        while time.perf_counter() < t_load:
-            step(bufs[0])
-        torch.cuda.synchronize()
         clk = clocks.stop()
     if world > 1:
         t = torch.tensor([ms], device=dev)
