@@ -417,8 +417,8 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         int kept = 0;
         const unsigned cap = (unsigned)K * (unsigned)K + 2u * K + 8u;
         int row = w.queue[0];
-        while (head < (unsigned)nfree) {
-            if (++visits > cap) { failed = true; break; }
+        while (head < (unsigned)nfree && visits < cap) {
+            ++visits;
             ++head;
             // the next queued row; push-backs only write consumed slots
             const int queued = w.queue[head < (unsigned)nfree ? head : 0];
@@ -509,7 +509,12 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 }
             }
             int j2 = -2;  // -2: not computed yet
-            if (!(v2 < kBig)) {
+            // the owner lane's price and row of j1 are fetched before the rare
+            // LARGE check, which would otherwise sit on the critical path
+            int l1 = L::lane_of(j1), s1 = L::slot_of(j1);
+            float vj1 = __shfl_sync(kFull, sel(v, s1), l1);
+            int i0 = __shfl_sync(kFull, seli(yc, s1), l1);
+            if (__builtin_expect(!(v2 < kBig), 0)) {
                 // a reduced cost at or above LARGE: replay the scalar scan
                 // of :193-210 exactly (its result is not the plain top-2 then)
 #pragma unroll
@@ -533,10 +538,11 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 v1 = __shfl_sync(kFull, va, 0);
                 v2 = __shfl_sync(kFull, vb, 0);
                 __syncwarp();
+                l1 = L::lane_of(j1);
+                s1 = L::slot_of(j1);
+                vj1 = __shfl_sync(kFull, sel(v, s1), l1);
+                i0 = __shfl_sync(kFull, seli(yc, s1), l1);
             }
-            const int l1 = L::lane_of(j1), s1 = L::slot_of(j1);
-            const float vj1 = __shfl_sync(kFull, sel(v, s1), l1);
-            int i0 = __shfl_sync(kFull, seli(yc, s1), l1);
             const float lowered = vj1 - (v2 - v1);
             const bool lowers = lowered < vj1;
             int jsel = j1;
@@ -567,15 +573,18 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 if (lane == ls) seti(yc, ss, row);
             }
             if (use_cache && own1) w.vsh[j1] = lowered;
-            if (lane == 0) {
-                w.xrow[row] = jsel;
-                if (push_back) w.queue[kept] = (int16_t)i0;
-            }
+            // every lane stores the same word: no divergent branch
+            w.xrow[row] = jsel;
+            if (push_back) w.queue[kept] = (int16_t)i0;
             kept += push_back;
             head -= push_front;
             row = push_front ? i0 : queued;
             if (use_cache) __syncwarp();  // cache / price mirror writes visible
         }
+#ifdef TMJV_PHASE_CLOCKS
+        if (lane == 0) atomicAdd(&tmjv_phase_cycles[5], (unsigned long long)visits);
+#endif
+        if (head < (unsigned)nfree) failed = true;  // loop bound reached
         nfree = kept;
         __syncwarp();
     }

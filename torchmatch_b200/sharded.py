@@ -108,6 +108,31 @@ def merge_words(words: list[int], group=None, device=None) -> list[int]:
     return t.cpu().tolist()
 
 
+def _merged_device_words(c: torch.Tensor, group=None) -> list[int]:
+    """Statistics of the local slice, merged across ranks with one host sync:
+    the five words are formed on the device and all-reduced there (NCCL);
+    with a CPU backend (gloo) they travel through the host instead."""
+    import torch.distributed as dist
+
+    if dist.get_backend(group) != "nccl":
+        words = _local_stats(c) if c.numel() else [0, 0, 0, 0, 0]
+        return merge_words(words, group)
+    t = torch.zeros(5, dtype=torch.int64, device=c.device)
+    if c.numel():
+        lib = _loader.core()
+        st = torch.empty(lib.tm_jv_workspace_bytes() // 4, dtype=torch.int32, device=c.device)
+        rc = lib.tm_jv_stats_f32(c.data_ptr(), c.numel(), st.data_ptr(), _stream(c.device))
+        if rc != 0:
+            raise RuntimeError("jonker_dense_batch statistics: "
+                               + lib.tm_status_string(rc).decode())
+        raw = st[:2].to(torch.int64) & 0xFFFFFFFF
+        # flag bits 1, 2, 4, 8 (NaN, -inf, finite, +inf) -> words 0..3
+        t[:4] = (raw[0] >> torch.arange(4, device=c.device)) & 1
+        t[4] = raw[1]
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return t.cpu().tolist()
+
+
 def solve_sharded(local: torch.Tensor, group=None) -> torch.Tensor:
     """Solve this rank's contiguous slice (B_r, N, M) of one global batch.
 
@@ -120,8 +145,7 @@ def solve_sharded(local: torch.Tensor, group=None) -> torch.Tensor:
     k = max(c.size(1), c.size(2))
     if k > _loader.core().tm_jv_max_k():
         raise RuntimeError(f"Batched JV (CUDA) supports max(N, M) <= 256, got K={k}")
-    words = _local_stats(c) if c.numel() else [0, 0, 0, 0, 0]
-    sentinel, pinf = sentinel_from_words(merge_words(words, group, c.device), k)
+    sentinel, pinf = sentinel_from_words(_merged_device_words(c, group), k)
     if c.size(2) == 0:
         return torch.full((c.size(0), c.size(1)), -1, dtype=torch.long, device=c.device)
     return _solve_local(c, sentinel, pinf)
