@@ -402,7 +402,10 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     // value stays below the bound, the cached columns hold the exact
     // lexicographic top-2 of the row and the row need not be read again.
     constexpr bool kCached = !TILE;
-    const bool use_cache = kCached && K > kCache;
+    // only wide rows pay for the cache: with K < 192 a miss (row scan + top-5
+    // extraction) costs more than the reads it saves (low hit rates on tied
+    // or masked costs)
+    const bool use_cache = kCached && K >= 192;
     if (use_cache) {
 #pragma unroll
         for (int s = 0; s < S; ++s) {
