@@ -565,15 +565,10 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             // branch-free register updates of the owner lanes
             const bool own1 = early && lowers && lane == l1;
             const int ls = L::lane_of(jsel), ss = L::slot_of(jsel);
-            if constexpr (S <= 2) {
 #pragma unroll
-                for (int t = 0; t < S; ++t) {
-                    v[t] = (own1 && t == s1) ? lowered : v[t];
-                    yc[t] = (lane == ls && t == ss) ? row : yc[t];
-                }
-            } else {
-                if (own1) setf(v, s1, lowered);
-                if (lane == ls) seti(yc, ss, row);
+            for (int t = 0; t < S; ++t) {
+                v[t] = (own1 && t == s1) ? lowered : v[t];
+                yc[t] = (lane == ls && t == ss) ? row : yc[t];
             }
             if (use_cache && own1) w.vsh[j1] = lowered;
             // every lane stores the same word: no divergent branch
@@ -843,7 +838,7 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
 
 // ------------------------------------------------------------------ kernel
 template <int S, int VEC, bool TILE, bool FULL>
-__global__ void __launch_bounds__(TILE ? 512 : 256, TILE ? 1 : (S > 4 ? 2 : 4)) jv_batch_kernel(const Params P) {
+__global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ? 1 : 4) jv_batch_kernel(const Params P) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
@@ -1014,7 +1009,7 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     P.warp_bytes = warp_bytes;
     P.tile_floats = tile_floats;
     int wpb = kSmemLimit / warp_bytes;
-    if (wpb > (TILE ? kMaxWarpsPerBlock : 8)) wpb = TILE ? kMaxWarpsPerBlock : 8;
+    if (wpb > ((TILE || S > 4) ? kMaxWarpsPerBlock : 8)) wpb = (TILE || S > 4) ? kMaxWarpsPerBlock : 8;
     if (wpb < 1) return TM_ERR_TOO_LARGE;
     const int64_t need_warps = P.B;
     if ((int64_t)wpb > need_warps) wpb = (int)need_warps;
