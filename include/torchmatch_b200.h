@@ -97,6 +97,16 @@ int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
                     int has_pos_inf, int64_t *out, void *workspace,
                     tm_stream_t stream);
 
+/* One pass that solves every problem whose cells are all finite and, in the
+ * same read, accumulates the batch statistics into workspace->stats (zeroed
+ * first).  Problems holding NaN, -inf or +inf are left as rows of -1: after
+ * reading the statistics back, the caller raises on NaN / -inf or, if the
+ * batch holds +inf, calls tm_jv_solve_f32 with the sentinel.  Together this
+ * replaces the separate statistics pass of the reference
+ * (cuda/cuda_common.cuh:215-255) for batches without +inf. */
+int tm_jv_solve_checked_f32(const float *costs, int64_t B, int N, int M, int64_t *out,
+                            void *workspace, tm_stream_t stream);
+
 /* Bytes of device scratch (a tm_jv_workspace) for tm_jv_solve_f32 and
  * tm_jonker_dense_batch_f32. */
 size_t tm_jv_workspace_bytes(void);

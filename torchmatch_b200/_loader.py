@@ -74,6 +74,8 @@ def core() -> ctypes.CDLL:
     lib.tm_jv_stats_f32.argtypes = [vp, i64, vp, vp]
     lib.tm_jv_sentinel.argtypes = [vp, i32, vp, vp]
     lib.tm_jv_solve_f32.argtypes = [vp, i64, i32, i32, ctypes.c_float, i32, vp, vp, vp]
+    lib.tm_jv_solve_checked_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
+    lib.tm_jv_solve_checked_f32.restype = i32
     lib.tm_jv_workspace_bytes.restype = ctypes.c_size_t
     lib.tm_jonker_dense_batch_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
     lib.tm_jonker_dense_batch_f32_noalloc.argtypes = [vp, i64, i32, i32, vp, vp]
@@ -92,6 +94,7 @@ EXPORTED = (
     "tm_jv_stats_f32",
     "tm_jv_sentinel",
     "tm_jv_solve_f32",
+    "tm_jv_solve_checked_f32",
     "tm_jv_workspace_bytes",
     "tm_jonker_dense_batch_f32",
     "tm_jonker_dense_batch_f32_noalloc",

@@ -65,10 +65,34 @@ struct Params {
     int64_t *out;
     int32_t *status;
     unsigned long long *ticket;  // next unclaimed problem (zeroed per launch)
+    tm_jv_stats *stats;          // check mode: batch statistics accumulate here
+    int check;                   // check mode: classify cells, bail on non-finite
     int warp_bytes;      // shared-memory bytes per warp
     int tile_floats;     // floats reserved for the staged tile (TILE mode)
     int bulk_ok;         // tile base and size are 16-byte multiples
 };
+
+// ------------------------------------------------------------- statistics
+__device__ __forceinline__ uint32_t order_key(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__host__ __device__ inline float key_to_float(uint32_t k) {
+    const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(u);
+#else
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+#endif
+}
+
+__device__ __forceinline__ void classify(float x, uint32_t &fl, uint32_t &mk) {
+    if (isnan(x)) fl |= TM_STAT_NAN;
+    else if (isinf(x)) fl |= x < 0.0f ? TM_STAT_NEG_INF : TM_STAT_POS_INF;
+    else { fl |= TM_STAT_FINITE; mk = max(mk, order_key(x)); }
+}
 
 // ---------------------------------------------------------------- warp ops
 __device__ __forceinline__ float warp_min_f(float x) {
@@ -295,11 +319,13 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
 
     // ---- column reduction (jonker_dense_flat.h:129-144) -------------------
     int ymin[S];
+    uint32_t chk_fl = 0, chk_mk = 0;  // check mode: cell classes, max finite key
 #pragma unroll
     for (int s = 0; s < S; ++s) { v[s] = kBig; ymin[s] = 0; }
     {
         const int nreal = N < K ? N : K;
         int i = 0;
+        const bool check = P.check != 0;
         for (; i + 2 <= nreal; i += 2) {
             float c0[S], c1[S];
             load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c0);
@@ -309,17 +335,48 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 if (c0[s] < v[s]) { v[s] = c0[s]; ymin[s] = i; }
                 if (c1[s] < v[s]) { v[s] = c1[s]; ymin[s] = i + 1; }
             }
+            if (check) {
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if (FULL || jj[s] < M) {
+                        classify(c0[s], chk_fl, chk_mk);
+                        classify(c1[s], chk_fl, chk_mk);
+                    }
+            }
         }
         for (; i < nreal; ++i) {
             load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c);
 #pragma unroll
             for (int s = 0; s < S; ++s)
                 if (c[s] < v[s]) { v[s] = c[s]; ymin[s] = i; }
+            if (check) {
+#pragma unroll
+                for (int s = 0; s < S; ++s)
+                    if (FULL || jj[s] < M) classify(c[s], chk_fl, chk_mk);
+            }
         }
         if (N < K) {  // first all-zero padding row; later ones never win (<)
 #pragma unroll
             for (int s = 0; s < S; ++s)
                 if (0.0f < v[s]) { v[s] = 0.0f; ymin[s] = N; }
+        }
+    }
+    if (P.check) {
+        // Check mode (no sentinel known yet): the column reduction above read
+        // every real cell once and classified it.  A problem holding a NaN,
+        // -inf or +inf cell stops here: its mapping needs the sentinel (and
+        // NaN / -inf are rejected anyway), so the host re-runs the batch with
+        // the sentinel or raises.
+        const uint32_t fl = __reduce_or_sync(kFull, chk_fl);
+        const uint32_t mk = __reduce_max_sync(kFull, chk_mk);
+        if (lane == 0) {
+            if (fl) atomicOr(&P.stats->flags, fl);
+            if (mk) atomicMax(&P.stats->max_key, mk);
+        }
+        if (fl & (TM_STAT_NAN | TM_STAT_NEG_INF | TM_STAT_POS_INF)) {
+            int64_t *ob = P.out + b * (int64_t)N;
+            for (int r = lane; r < N; r += 32) ob[r] = -1;
+            return;
         }
     }
 
@@ -629,25 +686,32 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     dv[s] = inf;
                     if (p >= lo && p < K) dv[s] = w.dist[w.order[p]];
                 }
+                // prefix minima over positions: the S per-slot scans are
+                // independent (run interleaved), then chained by their totals
+                float incl[S];
+#pragma unroll
+                for (int s = 0; s < S; ++s) incl[s] = dv[s];
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+#pragma unroll
+                    for (int s = 0; s < S; ++s) {
+                        const float t = __shfl_up_sync(kFull, incl[s], off);
+                        if (lane >= off) incl[s] = fminf(incl[s], t);
+                    }
+                }
                 float carry = inf;
                 unsigned evm[S], rsm[S];
 #pragma unroll
                 for (int s = 0; s < S; ++s) {
                     const int p = s * 32 + lane;
-                    float incl = dv[s];
-#pragma unroll
-                    for (int off = 1; off < 32; off <<= 1) {
-                        const float t = __shfl_up_sync(kFull, incl, off);
-                        if (lane >= off) incl = fminf(incl, t);
-                    }
-                    float excl = __shfl_up_sync(kFull, incl, 1);
+                    float excl = __shfl_up_sync(kFull, incl[s], 1);
                     excl = lane == 0 ? carry : fminf(carry, excl);
                     const bool live = p > lo && p < K;
                     const bool rst = live && dv[s] < excl;
                     const bool tie = live && dv[s] == excl;
                     rsm[s] = __ballot_sync(kFull, rst);
                     evm[s] = __ballot_sync(kFull, rst || tie);
-                    carry = fminf(carry, __shfl_sync(kFull, incl, 31));
+                    carry = fminf(carry, __shfl_sync(kFull, incl[s], 31));
                 }
                 mind = carry;
                 int nh = lo + 1;
@@ -894,28 +958,6 @@ __global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ?
     }
 }
 
-// ------------------------------------------------------------- statistics
-__device__ __forceinline__ uint32_t order_key(float f) {
-    const uint32_t u = __float_as_uint(f);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__host__ __device__ inline float key_to_float(uint32_t k) {
-    const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
-#ifdef __CUDA_ARCH__
-    return __uint_as_float(u);
-#else
-    float f;
-    memcpy(&f, &u, 4);
-    return f;
-#endif
-}
-
-__device__ __forceinline__ void classify(float x, uint32_t &fl, uint32_t &mk) {
-    if (isnan(x)) fl |= TM_STAT_NAN;
-    else if (isinf(x)) fl |= x < 0.0f ? TM_STAT_NEG_INF : TM_STAT_POS_INF;
-    else { fl |= TM_STAT_FINITE; mk = max(mk, order_key(x)); }
-}
-
 __global__ void __launch_bounds__(256) jv_stats_kernel(const float *__restrict__ x, int64_t n,
                                                        tm_jv_stats *out) {
     uint32_t fl = 0, mk = 0;
@@ -1123,8 +1165,9 @@ int tm_jv_sentinel(const tm_jv_stats *st, int K, float *sentinel, int *has_pos_i
     return TM_OK;
 }
 
-int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
-                    int has_pos_inf, int64_t *out, void *workspace, tm_stream_t stream_) {
+static int solve_impl(const float *costs, int64_t B, int N, int M, float sentinel,
+                      int has_pos_inf, int check, int64_t *out, void *workspace,
+                      tm_stream_t stream_) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
     if (B == 0 || N == 0) return TM_OK;
@@ -1133,13 +1176,17 @@ int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
     if (K > 32 * tmjv::kMaxSlots) return TM_ERR_TOO_LARGE;
     tmjv::StreamDevice scope(stream);
     if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
+    tm_jv_workspace *ws = reinterpret_cast<tm_jv_workspace *>(workspace);
+    // check mode starts the statistics from zero; a plain solve keeps them
+    void *zero_from = check ? static_cast<void *>(&ws->stats) : static_cast<void *>(&ws->ticket);
+    const size_t zero_bytes = check ? sizeof(ws->stats) + sizeof(ws->ticket) + sizeof(ws->status)
+                                    : sizeof(ws->ticket) + sizeof(ws->status);
+    cudaError_t e = cudaMemsetAsync(zero_from, 0, zero_bytes, stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
     if (M == 0) {
-        cudaError_t e = cudaMemsetAsync(out, 0xff, sizeof(int64_t) * (size_t)B * N, stream);
+        e = cudaMemsetAsync(out, 0xff, sizeof(int64_t) * (size_t)B * N, stream);
         return e == cudaSuccess ? TM_OK : tmjv::cuda_fail(e);
     }
-    tm_jv_workspace *ws = reinterpret_cast<tm_jv_workspace *>(workspace);
-    cudaError_t e = cudaMemsetAsync(&ws->ticket, 0, sizeof(ws->ticket) + sizeof(ws->status), stream);
-    if (e != cudaSuccess) return tmjv::cuda_fail(e);
     tmjv::Params P{};
     P.costs = costs;
     P.B = B;
@@ -1147,11 +1194,23 @@ int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
     P.M = M;
     P.K = K;
     P.sentinel = sentinel;
-    P.sanitize = has_pos_inf ? 1 : 0;
+    P.sanitize = (has_pos_inf && !check) ? 1 : 0;
+    P.check = check;
+    P.stats = &ws->stats;
     P.out = out;
     P.status = &ws->status;
     P.ticket = &ws->ticket;
     return tmjv::launch(P, stream);
+}
+
+int tm_jv_solve_f32(const float *costs, int64_t B, int N, int M, float sentinel,
+                    int has_pos_inf, int64_t *out, void *workspace, tm_stream_t stream_) {
+    return solve_impl(costs, B, N, M, sentinel, has_pos_inf, 0, out, workspace, stream_);
+}
+
+int tm_jv_solve_checked_f32(const float *costs, int64_t B, int N, int M, int64_t *out,
+                            void *workspace, tm_stream_t stream_) {
+    return solve_impl(costs, B, N, M, 0.0f, 0, 1, out, workspace, stream_);
 }
 
 size_t tm_jv_workspace_bytes(void) { return sizeof(tm_jv_workspace); }
@@ -1162,15 +1221,16 @@ int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64
     if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
     if (B == 0 || N == 0) return TM_OK;
     if (!out || !workspace) return TM_ERR_ARG;
-    tmjv::StreamDevice scope(stream);
-    if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
-    if (M == 0) return tm_jv_solve_f32(costs, B, N, M, 0.0f, 0, out, workspace, stream_);
     const int K = N > M ? N : M;
     if (K > tm_jv_max_k()) return TM_ERR_TOO_LARGE;
-    tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
-    int rc = tm_jv_stats_f32(costs, B * (int64_t)N * M, st, stream_);
+    if (M == 0) return tm_jv_solve_f32(costs, B, N, M, 0.0f, 0, out, workspace, stream_);
+    tmjv::StreamDevice scope(stream);
+    if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
+    // one pass solves every all-finite problem and gathers the statistics
+    int rc = tm_jv_solve_checked_f32(costs, B, N, M, out, workspace, stream_);
     if (rc) return rc;
     tm_jv_stats h{};
+    const tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
     cudaError_t e = cudaMemcpyAsync(&h, st, sizeof(h), cudaMemcpyDeviceToHost, stream);
     if (e != cudaSuccess) return tmjv::cuda_fail(e);
     e = cudaStreamSynchronize(stream);
@@ -1179,7 +1239,9 @@ int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64
     int pinf = 0;
     rc = tm_jv_sentinel(&h, K, &sentinel, &pinf);
     if (rc) return rc;
-    return tm_jv_solve_f32(costs, B, N, M, sentinel, pinf, out, workspace, stream_);
+    // +inf cells need the batch-global sentinel: solve again with it
+    if (pinf) return tm_jv_solve_f32(costs, B, N, M, sentinel, 1, out, workspace, stream_);
+    return TM_OK;
 }
 
 }  // extern "C"

@@ -10,7 +10,8 @@
 // Behaviour kept from jonker_dense_batch_cuda (cuda/dispatch.cu:137-177):
 // device guard, current-stream execution, refusal inside CUDA graph capture,
 // fp32 cast, batch-global +inf sentinel with a host sync to raise on NaN /
-// -inf, a fresh int64 (B, N) output.  Widened: rectangular (B, N, M) input
+// -inf, a fresh int64 (B, N) output.  The statistics come out of the solve
+// itself (check mode); only batches holding +inf are solved a second time.  Widened: rectangular (B, N, M) input
 // and max(N, M) up to tm_jv_max_k(); non-contiguous input is made
 // contiguous instead of rejected.  All device work goes through the C ABI in
 // include/torchmatch_b200.h.
@@ -72,8 +73,14 @@ at::Tensor jonker_dense_batch_cuda(const at::Tensor &costs) {
         at::empty({(int64_t)tm_jv_workspace_bytes()}, c.options().dtype(at::kByte));
     auto *ws = reinterpret_cast<tm_jv_workspace *>(scratch.mutable_data_ptr());
     auto *st_dev = &ws->stats;
-    int rc = tm_jv_stats_f32(cp, c.numel(), st_dev, stream_h);
-    TORCH_CHECK(rc == TM_OK, "batched JV statistics failed: ", status_text(rc));
+    // one pass solves every all-finite problem and gathers the statistics;
+    // the host then raises on NaN / -inf (reference cuda_common.cuh:245-249)
+    // or, if the batch holds +inf, solves again with the global sentinel
+    at::Tensor out = at::empty({B, N}, costs.options().dtype(at::kLong));
+    int64_t *op = out.mutable_data_ptr<int64_t>();
+    int rc = tm_jv_solve_checked_f32(cp, B, static_cast<int>(N), static_cast<int>(M), op, ws,
+                                     stream_h);
+    TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
     tm_jv_stats host{};
     cudaError_t e =
         cudaMemcpyAsync(&host, st_dev, sizeof(host), cudaMemcpyDeviceToHost, stream);
@@ -86,11 +93,11 @@ at::Tensor jonker_dense_batch_cuda(const at::Tensor &costs) {
     TORCH_CHECK(rc != TM_ERR_NAN, "jonker_dense_batch: ", tm_status_string(rc));
     TORCH_CHECK(rc != TM_ERR_NEG_INF, "jonker_dense_batch: ", tm_status_string(rc));
     TORCH_CHECK(rc == TM_OK, "jonker_dense_batch: ", status_text(rc));
-
-    at::Tensor out = at::empty({B, N}, costs.options().dtype(at::kLong));
-    rc = tm_jv_solve_f32(cp, B, static_cast<int>(N), static_cast<int>(M), sentinel, has_pos_inf,
-                         out.mutable_data_ptr<int64_t>(), ws, stream_h);
-    TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
+    if (has_pos_inf) {
+        rc = tm_jv_solve_f32(cp, B, static_cast<int>(N), static_cast<int>(M), sentinel, 1, op,
+                             ws, stream_h);
+        TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
+    }
     return out;
 }
 

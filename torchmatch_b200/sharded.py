@@ -108,47 +108,58 @@ def merge_words(words: list[int], group=None, device=None) -> list[int]:
     return t.cpu().tolist()
 
 
-def _merged_device_words(c: torch.Tensor, group=None) -> list[int]:
-    """Statistics of the local slice, merged across ranks with one host sync:
-    the five words are formed on the device and all-reduced there (NCCL);
-    with a CPU backend (gloo) they travel through the host instead."""
-    import torch.distributed as dist
-
-    if dist.get_backend(group) != "nccl":
-        words = _local_stats(c) if c.numel() else [0, 0, 0, 0, 0]
-        return merge_words(words, group)
-    t = torch.zeros(5, dtype=torch.int64, device=c.device)
-    if c.numel():
-        lib = _loader.core()
-        st = torch.empty(lib.tm_jv_workspace_bytes() // 4, dtype=torch.int32, device=c.device)
-        rc = lib.tm_jv_stats_f32(c.data_ptr(), c.numel(), st.data_ptr(), _stream(c.device))
-        if rc != 0:
-            raise RuntimeError("jonker_dense_batch statistics: "
-                               + lib.tm_status_string(rc).decode())
-        raw = st[:2].to(torch.int64) & 0xFFFFFFFF
-        # flag bits 1, 2, 4, 8 (NaN, -inf, finite, +inf) -> words 0..3
-        t[:4] = (raw[0] >> torch.arange(4, device=c.device)) & 1
-        t[4] = raw[1]
-    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
-    return t.cpu().tolist()
+def _device_words(st: torch.Tensor) -> torch.Tensor:
+    """tm_jv_stats (first two int32 of a workspace) -> the five int64 words."""
+    raw = st[:2].to(torch.int64) & 0xFFFFFFFF
+    t = torch.empty(5, dtype=torch.int64, device=st.device)
+    # flag bits 1, 2, 4, 8 (NaN, -inf, finite, +inf) -> words 0..3
+    t[:4] = (raw[0] >> torch.arange(4, device=st.device)) & 1
+    t[4] = raw[1]
+    return t
 
 
 def solve_sharded(local: torch.Tensor, group=None) -> torch.Tensor:
     """Solve this rank's contiguous slice (B_r, N, M) of one global batch.
 
-    Collective over ``group`` (every rank calls it with the same N, M).
-    Returns the (B_r, N) int64 mapping of the local slice.
+    Collective over ``group`` (every rank calls it with the same N, M).  The
+    slice is solved in check mode, which also yields its statistics; one
+    all-reduce merges them, the host raises on NaN / -inf anywhere, and only
+    if some slice holds +inf is the slice solved again with the global
+    sentinel.  Returns the (B_r, N) int64 mapping of the local slice.
     """
+    import torch.distributed as dist
+
     if local.dim() != 3:
         raise RuntimeError("costs must be 3D (B, N, M)")
     c = local.to(torch.float32).contiguous()
-    k = max(c.size(1), c.size(2))
-    if k > _loader.core().tm_jv_max_k():
+    b, n, m = c.shape
+    k = max(n, m)
+    lib = _loader.core()
+    if k > lib.tm_jv_max_k():
         raise RuntimeError(f"Batched JV (CUDA) supports max(N, M) <= 256, got K={k}")
-    sentinel, pinf = sentinel_from_words(_merged_device_words(c, group), k)
-    if c.size(2) == 0:
-        return torch.full((c.size(0), c.size(1)), -1, dtype=torch.long, device=c.device)
-    return _solve_local(c, sentinel, pinf)
+    ws = torch.zeros(lib.tm_jv_workspace_bytes() // 4, dtype=torch.int32, device=c.device)
+    out = torch.full((b, n), -1, dtype=torch.long, device=c.device)
+    if b and n and m:
+        rc = lib.tm_jv_solve_checked_f32(c.data_ptr(), b, n, m, out.data_ptr(), ws.data_ptr(),
+                                         _stream(c.device))
+        if rc != 0:
+            raise RuntimeError("batched JV kernel launch failed: "
+                               + lib.tm_status_string(rc).decode())
+    if dist.get_backend(group) == "nccl":
+        t = _device_words(ws)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        words = t.cpu().tolist()
+    else:
+        flags, key = (int(v) & 0xFFFFFFFF for v in ws[:2].cpu().tolist())
+        words = merge_words(stats_words(flags, key), group)
+    sentinel, pinf = sentinel_from_words(words, k)
+    if pinf and b and n and m:
+        rc = lib.tm_jv_solve_f32(c.data_ptr(), b, n, m, sentinel, 1, out.data_ptr(),
+                                 ws.data_ptr(), _stream(c.device))
+        if rc != 0:
+            raise RuntimeError("batched JV kernel launch failed: "
+                               + lib.tm_status_string(rc).decode())
+    return out
 
 
 def shard_bounds(b: int, parts: int) -> list[tuple[int, int]]:
