@@ -132,6 +132,25 @@ int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M,
 int tm_jonker_dense_batch_f32_noalloc(const float *costs, int64_t B, int N, int M,
                                       int64_t *out, tm_stream_t stream);
 
+/* Device outputs of jonker_dense_batch_unpacked (cpu/ops.cpp:290-295):
+ * matches (B, N, 2) matched (row, column) pairs in row order, valid in
+ * [0, n_matched[b]); unmatched_rows (B, N), valid in [0, N - n_matched[b]);
+ * unmatched_cols (B, M) in column order, valid in [0, M - n_matched[b]);
+ * n_matched (B,).  Every entry past its count is -1. */
+typedef struct tm_jv_unpacked {
+    int64_t *matches;
+    int64_t *unmatched_rows;
+    int64_t *unmatched_cols;
+    int64_t *n_matched;
+} tm_jv_unpacked;
+
+/* jonker_dense_batch_unpacked for N, M >= 1: the same solve as
+ * tm_jonker_dense_batch_f32 with the compaction written by the solve kernel
+ * itself.  Replaces cpu/ops.cpp:297-417 (the reference has it on CPU only). */
+int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int M,
+                                       const tm_jv_unpacked *u, void *workspace,
+                                       tm_stream_t stream);
+
 /* The cudaError_t of the last TM_ERR_CUDA on this thread. */
 int tm_last_cuda_error(void);
 

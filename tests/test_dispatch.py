@@ -154,3 +154,8 @@ def test_fake_kernel_shape():
     with FakeTensorMode():
         out = torch.ops.assignment.jonker_dense_batch(torch.empty(3, 5, 7))
     assert out.shape == (3, 5) and out.dtype == torch.long
+
+
+def test_cuda_unpack_uses_native_unpacked_op(record_ops):
+    solve(FakeCuda(2, 8, 12), unpack=True)
+    assert record_ops == [("jonker_dense_batch_unpacked", (2, 8, 12))]

@@ -220,3 +220,56 @@ def test_stats_kernel(oracle_mod):
         mx = np.frombuffer(np.uint32(u).tobytes(), np.float32)[0]
         fin = y.numpy()[np.isfinite(y.numpy())]
         assert mx == fin.max()
+
+
+def _unpack_like_reference(packed: np.ndarray, m: int):
+    """cpu/ops.cpp:378-414 restated: pairs in row order, unmatched rows, unused
+    columns in column order, -1 past every count."""
+    b, n = packed.shape
+    mt = np.full((b, n, 2), -1, np.int64)
+    ur = np.full((b, n), -1, np.int64)
+    uc = np.full((b, m), -1, np.int64)
+    nm = np.zeros(b, np.int64)
+    for k in range(b):
+        rows = np.nonzero(packed[k] >= 0)[0]
+        nm[k] = len(rows)
+        mt[k, : len(rows), 0] = rows
+        mt[k, : len(rows), 1] = packed[k, rows]
+        miss = np.nonzero(packed[k] < 0)[0]
+        ur[k, : len(miss)] = miss
+        free = np.setdiff1d(np.arange(m), packed[k, rows])
+        uc[k, : len(free)] = free
+    return mt, ur, uc, nm
+
+
+@pytest.mark.parametrize("name", ["config4_b256", "tall9x5", "wide5x9", "ties_small",
+                                  "gated32", "rect250x6", "sq256", "inf_known_answer"])
+def test_unpacked_matches_reference_layout(name, golden):
+    outs, _ = golden
+    x = CASES[name]()
+    got = torch.ops.assignment.jonker_dense_batch_unpacked(x.cuda())
+    want = _unpack_like_reference(outs[name], x.shape[2])
+    for g, w in zip(got, want):
+        np.testing.assert_array_equal(g.cpu().numpy(), w)
+
+
+def test_unpacked_empty_and_errors():
+    op = torch.ops.assignment.jonker_dense_batch_unpacked
+    m, ur, uc, nm = op(torch.zeros(3, 0, 4, device="cuda"))
+    assert m.shape == (3, 0, 2) and uc.shape == (3, 4) and nm.tolist() == [0, 0, 0]
+    bad = torch.ones(2, 3, 3, device="cuda")
+    bad[1, 2, 0] = float("nan")
+    with pytest.raises(RuntimeError, match="NaN"):
+        op(bad)
+
+
+def test_unpacked_opcheck_and_solve_route():
+    from torchmatch_b200.assignment import solve
+
+    x = torch.rand(4, 12, 17, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
+    torch.library.opcheck(torch.ops.assignment.jonker_dense_batch_unpacked, (x,),
+                          test_utils=("test_schema", "test_faketensor"))
+    native = solve(x, unpack=True)
+    packed = solve(x).cpu().numpy()
+    for g, w in zip(native, _unpack_like_reference(packed, 17)):
+        np.testing.assert_array_equal(g.cpu().numpy(), w)

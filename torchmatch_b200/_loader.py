@@ -30,13 +30,15 @@ TORCH_LIB = LIBDIR / "libtmjv_torch.so"
 
 OP = "assignment::jonker_dense_batch"
 SCHEMA = "(Tensor costs) -> Tensor"
+OP_UNPACKED = "assignment::jonker_dense_batch_unpacked"
+SCHEMA_UNPACKED = "(Tensor costs) -> (Tensor, Tensor, Tensor, Tensor)"
 
 _LIB_HANDLES: list[object] = []
 
 
-def _has_op() -> bool:
+def _has_op(name: str = OP) -> bool:
     try:
-        torch._C._dispatch_find_schema_or_throw(OP, "")
+        torch._C._dispatch_find_schema_or_throw(name, "")
         return True
     except RuntimeError:
         return False
@@ -47,6 +49,17 @@ def _fake(costs: torch.Tensor) -> torch.Tensor:
     return costs.new_empty(costs.size(0), costs.size(1), dtype=torch.long)
 
 
+def _fake_unpacked(costs: torch.Tensor):
+    torch._check(costs.dim() == 3, lambda: "costs must be 3D (B, N, M)")
+    b, n, m = costs.size(0), costs.size(1), costs.size(2)
+    return (
+        costs.new_empty(b, n, 2, dtype=torch.long),
+        costs.new_empty(b, n, dtype=torch.long),
+        costs.new_empty(b, m, dtype=torch.long),
+        costs.new_empty(b, dtype=torch.long),
+    )
+
+
 @functools.cache
 def load() -> None:
     """Define the op (if needed), register its fake and load the CUDA impl."""
@@ -54,14 +67,15 @@ def load() -> None:
         raise ImportError(
             f"{TORCH_LIB} is not built; run `python torchmatch_b200/_build.py`"
         )
-    if not _has_op():
-        lib = torch.library.Library("assignment", "FRAGMENT")
-        lib.define("jonker_dense_batch" + SCHEMA)
-        _LIB_HANDLES.append(lib)
-    try:
-        torch.library.register_fake(OP)(_fake)
-    except RuntimeError:
-        pass  # the reference's loader registered the same fake already
+    for name, schema, fake in ((OP, SCHEMA, _fake), (OP_UNPACKED, SCHEMA_UNPACKED, _fake_unpacked)):
+        if not _has_op(name):
+            lib = torch.library.Library("assignment", "FRAGMENT")
+            lib.define(name.split("::")[1] + schema)
+            _LIB_HANDLES.append(lib)
+        try:
+            torch.library.register_fake(name)(fake)
+        except RuntimeError:
+            pass  # the reference's loader registered the same fake already
     torch.ops.load_library(str(TORCH_LIB))
 
 
@@ -80,6 +94,8 @@ def core() -> ctypes.CDLL:
     lib.tm_jonker_dense_batch_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
     lib.tm_jonker_dense_batch_f32_noalloc.argtypes = [vp, i64, i32, i32, vp, vp]
     lib.tm_jonker_dense_batch_f32_noalloc.restype = i32
+    lib.tm_jonker_dense_batch_unpacked_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
+    lib.tm_jonker_dense_batch_unpacked_f32.restype = i32
     lib.tm_status_string.restype = ctypes.c_char_p
     lib.tm_status_string.argtypes = [i32]
     for name in ("tm_jv_stats_f32", "tm_jv_sentinel", "tm_jv_solve_f32",
@@ -98,6 +114,7 @@ EXPORTED = (
     "tm_jv_workspace_bytes",
     "tm_jonker_dense_batch_f32",
     "tm_jonker_dense_batch_f32_noalloc",
+    "tm_jonker_dense_batch_unpacked_f32",
     "tm_last_cuda_error",
     "tm_status_string",
 )

@@ -48,7 +48,7 @@ _OPS = types.SimpleNamespace(
     jonker_dense=_op("jonker_dense"),
     jonker_compact=_op("jonker_compact"),
     jonker_compact_batch=_op("jonker_compact_batch"),
-    jonker_dense_batch_unpacked=_op("jonker_dense_batch_unpacked"),
+    jonker_dense_batch_unpacked=torch.ops.assignment.jonker_dense_batch_unpacked,
     jonker_compact_batch_unpacked=_op("jonker_compact_batch_unpacked"),
     munkres=_op("munkres"),
     lawler=_op("lawler"),
@@ -106,6 +106,14 @@ def _dense_batch(cost: torch.Tensor) -> torch.Tensor:
     return _OPS.jonker_dense_batch(cost)
 
 
+def _dense_batch_result(cost: torch.Tensor, m: int, unpack: bool):
+    """CUDA 3-D: packed op, or the native unpacked op when unpack=True."""
+    if unpack and _ALLOW_NATIVE_UNPACK and _OPS.jonker_dense_batch_unpacked is not None:
+        return _OPS.jonker_dense_batch_unpacked(cost)
+    packed = _dense_batch(cost)
+    return _unpack_packed(packed, m) if unpack else packed
+
+
 def _dispatch_auto(cost: torch.Tensor, *, unpack: bool):
     is_cuda = cost.device.type == "cuda"
     if cost.ndim == 2:
@@ -123,8 +131,7 @@ def _dispatch_auto(cost: torch.Tensor, *, unpack: bool):
     if not is_cuda:
         return _dispatch_jonker(cost, unpack=unpack)
     if _cuda_batch_fits(n, m):
-        packed = _dense_batch(cost)
-        return _unpack_packed(packed, m) if unpack else packed
+        return _dense_batch_result(cost, m, unpack)
     op = _require(_pick_auto_cuda_2d(n))
     packed = torch.stack([op(cost[i]) for i in range(b)], dim=0)
     return _unpack_packed(packed, m) if unpack else packed
@@ -205,8 +212,7 @@ def _dispatch_jonker(cost: torch.Tensor, *, unpack: bool):
                 f"K <= {_CUDA_BATCH_MAX_K}, got K={max(n, m)}; transfer to CPU"
             )
             raise ValueError(msg)
-        packed = _dense_batch(cost)
-        return _unpack_packed(packed, m) if unpack else packed
+        return _dense_batch_result(cost, m, unpack)
     # CPU: the reference's own CPU ops, when its extension is loaded.
     if cost.ndim == 2:
         packed = _require(_pick_jonker_cpu_2d(cost.size(0), cost.size(1)))(cost)

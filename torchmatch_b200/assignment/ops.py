@@ -12,12 +12,13 @@ import torch
 _OPS = torch.ops.assignment
 
 jonker_dense_batch = _OPS.jonker_dense_batch
+jonker_dense_batch_unpacked = _OPS.jonker_dense_batch_unpacked
 
-__all__ = ["jonker_dense_batch"]
+__all__ = ["jonker_dense_batch", "jonker_dense_batch_unpacked"]
 
 for _name in (
     "jonker_scalar", "jonker_dense", "jonker_compact", "jonker_compact_batch",
-    "jonker_dense_batch_unpacked", "jonker_compact_batch_unpacked",
+    "jonker_compact_batch_unpacked",
     "munkres", "hybrid", "lawler", "greedy",
 ):
     if hasattr(_OPS, _name):

@@ -66,6 +66,11 @@ struct Params {
     int32_t *status;
     unsigned long long *ticket;  // next unclaimed problem (zeroed per launch)
     tm_jv_stats *stats;          // check mode: batch statistics accumulate here
+    // optional compacted outputs of jonker_dense_batch_unpacked (cpu/ops.cpp:290-417)
+    int64_t *um;                 // (B, N, 2) matched (row, column) pairs
+    int64_t *uur;                // (B, N) unmatched rows
+    int64_t *uuc;                // (B, M) unmatched columns
+    int64_t *unm;                // (B,) number of matches
     int check;                   // check mode: classify cells, bail on non-finite
     int warp_bytes;      // shared-memory bytes per warp
     int tile_floats;     // floats reserved for the staged tile (TILE mode)
@@ -290,6 +295,65 @@ __device__ __forceinline__ void load_row(const float *__restrict__ src, int i, i
     }
 }
 
+// Writes one problem's result: the packed row -> column mapping (column >= M
+// or unsolved -> -1, cpu/ops.cpp:274-283) and, when requested, the compacted
+// form of jonker_dense_batch_unpacked (cpu/ops.cpp:378-414): matched pairs in
+// row order, unmatched rows, unmatched columns in column order, the count,
+// and -1 in every position past the counts.
+__device__ void emit_result(const Params &P, WarpShared &w, int lane, int64_t b, int N, int M,
+                            bool valid) {
+    int64_t *ob = P.out ? P.out + b * (int64_t)N : nullptr;
+    if (!P.um) {
+        for (int r = lane; r < N; r += 32) {
+            const int x = valid ? w.xrow[r] : -1;
+            ob[r] = (x >= 0 && x < M) ? (int64_t)x : (int64_t)-1;
+        }
+        __syncwarp();
+        return;
+    }
+    const unsigned lt = (1u << lane) - 1;
+    for (int j = lane; j < M; j += 32) w.flag[j] = 0;
+    __syncwarp();
+    int64_t *mb = P.um + b * (int64_t)N * 2;
+    int64_t *urb = P.uur + b * (int64_t)N;
+    int64_t *ucb = P.uuc + b * (int64_t)M;
+    int nm = 0, nu = 0;
+    for (int r0 = 0; r0 < N; r0 += 32) {
+        const int r = r0 + lane;
+        int x = -1;
+        if (r < N) {
+            x = valid ? w.xrow[r] : -1;
+            if (!(x >= 0 && x < M)) x = -1;
+            if (ob) ob[r] = x;
+        }
+        const bool hit = r < N && x >= 0, miss = r < N && x < 0;
+        const unsigned bh = __ballot_sync(kFull, hit), bm = __ballot_sync(kFull, miss);
+        if (hit) {
+            const int k = nm + __popc(bh & lt);
+            mb[2 * k] = r;
+            mb[2 * k + 1] = x;
+            w.flag[x] = 1;
+        }
+        if (miss) urb[nu + __popc(bm & lt)] = r;
+        nm += __popc(bh);
+        nu += __popc(bm);
+    }
+    __syncwarp();
+    int nc = 0;
+    for (int j0 = 0; j0 < M; j0 += 32) {
+        const int j = j0 + lane;
+        const bool free_col = j < M && !w.flag[j];
+        const unsigned bf = __ballot_sync(kFull, free_col);
+        if (free_col) ucb[nc + __popc(bf & lt)] = j;
+        nc += __popc(bf);
+    }
+    for (int k = nm + lane; k < N; k += 32) { mb[2 * k] = -1; mb[2 * k + 1] = -1; }
+    for (int k = nu + lane; k < N; k += 32) urb[k] = -1;
+    for (int k = nc + lane; k < M; k += 32) ucb[k] = -1;
+    if (lane == 0) P.unm[b] = nm;
+    __syncwarp();
+}
+
 // ------------------------------------------------------------- one solve
 template <int S, int VEC, bool TILE, bool FULL>
 __device__ void solve_problem(const float *__restrict__ src, const Params &P, WarpShared &w,
@@ -374,8 +438,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             if (mk) atomicMax(&P.stats->max_key, mk);
         }
         if (fl & (TM_STAT_NAN | TM_STAT_NEG_INF | TM_STAT_POS_INF)) {
-            int64_t *ob = P.out + b * (int64_t)N;
-            for (int r = lane; r < N; r += 32) ob[r] = -1;
+            emit_result(P, w, lane, b, N, M, false);
             return;
         }
     }
@@ -854,13 +917,9 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
 
     TMJV_ACC(4, t_sp);
     // ---- output (cpu/ops.cpp:274-283) ------------------------------------
-    int64_t *ob = P.out + b * (int64_t)N;
-    for (int r = lane; r < N; r += 32) {
-        const int x = w.xrow[r];
-        ob[r] = (!failed && x >= 0 && x < M) ? (int64_t)x : (int64_t)-1;
-    }
-    if (failed && lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_ERR_UNSOLVED);
     __syncwarp();
+    emit_result(P, w, lane, b, N, M, !failed);
+    if (failed && lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_ERR_UNSOLVED);
 }
 
 // --------------------------------------------------------- TMA primitives
@@ -1167,11 +1226,13 @@ int tm_jv_sentinel(const tm_jv_stats *st, int K, float *sentinel, int *has_pos_i
 
 static int solve_impl(const float *costs, int64_t B, int N, int M, float sentinel,
                       int has_pos_inf, int check, int64_t *out, void *workspace,
-                      tm_stream_t stream_) {
+                      tm_stream_t stream_, const tm_jv_unpacked *u = nullptr) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
     if (B == 0 || N == 0) return TM_OK;
-    if (!out || !workspace || (M > 0 && !costs)) return TM_ERR_ARG;
+    if ((!out && !u) || !workspace || (M > 0 && !costs)) return TM_ERR_ARG;
+    if (u && (!u->matches || !u->unmatched_rows || !u->unmatched_cols || !u->n_matched))
+        return TM_ERR_ARG;
     const int K = N > M ? N : M;
     if (K > 32 * tmjv::kMaxSlots) return TM_ERR_TOO_LARGE;
     tmjv::StreamDevice scope(stream);
@@ -1184,8 +1245,12 @@ static int solve_impl(const float *costs, int64_t B, int N, int M, float sentine
     cudaError_t e = cudaMemsetAsync(zero_from, 0, zero_bytes, stream);
     if (e != cudaSuccess) return tmjv::cuda_fail(e);
     if (M == 0) {
-        e = cudaMemsetAsync(out, 0xff, sizeof(int64_t) * (size_t)B * N, stream);
-        return e == cudaSuccess ? TM_OK : tmjv::cuda_fail(e);
+        if (out) {
+            e = cudaMemsetAsync(out, 0xff, sizeof(int64_t) * (size_t)B * N, stream);
+            if (e != cudaSuccess) return tmjv::cuda_fail(e);
+        }
+        if (u) return TM_ERR_ARG;  // the unpacked op handles empty shapes itself
+        return TM_OK;
     }
     tmjv::Params P{};
     P.costs = costs;
@@ -1198,6 +1263,12 @@ static int solve_impl(const float *costs, int64_t B, int N, int M, float sentine
     P.check = check;
     P.stats = &ws->stats;
     P.out = out;
+    if (u) {
+        P.um = u->matches;
+        P.uur = u->unmatched_rows;
+        P.uuc = u->unmatched_cols;
+        P.unm = u->n_matched;
+    }
     P.status = &ws->status;
     P.ticket = &ws->ticket;
     return tmjv::launch(P, stream);
@@ -1241,6 +1312,33 @@ int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64
     if (rc) return rc;
     // +inf cells need the batch-global sentinel: solve again with it
     if (pinf) return tm_jv_solve_f32(costs, B, N, M, sentinel, 1, out, workspace, stream_);
+    return TM_OK;
+}
+
+int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int M,
+                                       const tm_jv_unpacked *u, void *workspace,
+                                       tm_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (B < 0 || N <= 0 || M <= 0) return B == 0 ? TM_OK : TM_ERR_ARG;
+    if (B == 0) return TM_OK;
+    if (!u || !workspace) return TM_ERR_ARG;
+    const int K = N > M ? N : M;
+    if (K > tm_jv_max_k()) return TM_ERR_TOO_LARGE;
+    tmjv::StreamDevice scope(stream);
+    if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
+    int rc = solve_impl(costs, B, N, M, 0.0f, 0, 1, nullptr, workspace, stream_, u);
+    if (rc) return rc;
+    tm_jv_stats h{};
+    const tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
+    cudaError_t e = cudaMemcpyAsync(&h, st, sizeof(h), cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    float sentinel = 1.0f;
+    int pinf = 0;
+    rc = tm_jv_sentinel(&h, K, &sentinel, &pinf);
+    if (rc) return rc;
+    if (pinf) return solve_impl(costs, B, N, M, sentinel, 1, 0, nullptr, workspace, stream_, u);
     return TM_OK;
 }
 

@@ -101,8 +101,46 @@ at::Tensor jonker_dense_batch_cuda(const at::Tensor &costs) {
     return out;
 }
 
+// jonker_dense_batch_unpacked on CUDA (the reference has it on CPU only,
+// cpu/ops.cpp:297-417): the same solve, with the compacted outputs written by
+// the solve kernel's output stage.  Layout and empty-shape behaviour follow
+// the CPU op (cpu/ops.cpp:290-316).
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor>
+jonker_dense_batch_unpacked_cuda(const at::Tensor &costs) {
+    TORCH_CHECK(costs.is_cuda(), "costs must be a CUDA tensor");
+    TORCH_CHECK(costs.dim() == 3, "costs must be 3D (B, N, M), got ", costs.dim());
+    TORCH_CHECK(costs.scalar_type() == at::kFloat || costs.scalar_type() == at::kDouble,
+                "costs must be float32 or float64, got ", costs.scalar_type());
+    const c10::cuda::CUDAGuard guard(costs.device());
+    const int64_t B = costs.size(0), N = costs.size(1), M = costs.size(2);
+    const auto lo = costs.options().dtype(at::kLong);
+    if (B == 0 || N == 0 || M == 0)
+        return {at::empty({B, N, 2}, lo), at::empty({B, N}, lo), at::empty({B, M}, lo),
+                at::zeros({B}, lo)};
+    const int64_t K = std::max(N, M);
+    TORCH_CHECK(K <= tm_jv_max_k(), "Batched JV (CUDA) supports max(N, M) <= ", tm_jv_max_k(),
+                ", got K=", K);
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+    check_not_capturing(stream, "jonker_dense_batch_unpacked");
+    const at::Tensor c = costs.to(at::kFloat).contiguous();
+    at::Tensor scratch =
+        at::empty({(int64_t)tm_jv_workspace_bytes()}, c.options().dtype(at::kByte));
+    at::Tensor matches = at::empty({B, N, 2}, lo), ur = at::empty({B, N}, lo);
+    at::Tensor uc = at::empty({B, M}, lo), nm = at::empty({B}, lo);
+    tm_jv_unpacked u{matches.mutable_data_ptr<int64_t>(), ur.mutable_data_ptr<int64_t>(),
+                     uc.mutable_data_ptr<int64_t>(), nm.mutable_data_ptr<int64_t>()};
+    const int rc = tm_jonker_dense_batch_unpacked_f32(
+        c.const_data_ptr<float>(), B, static_cast<int>(N), static_cast<int>(M), &u,
+        scratch.mutable_data_ptr(), reinterpret_cast<tm_stream_t>(stream));
+    TORCH_CHECK(rc != TM_ERR_NAN, "jonker_dense_batch_unpacked: ", tm_status_string(rc));
+    TORCH_CHECK(rc != TM_ERR_NEG_INF, "jonker_dense_batch_unpacked: ", tm_status_string(rc));
+    TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
+    return {matches, ur, uc, nm};
+}
+
 }  // namespace
 
 TORCH_LIBRARY_IMPL(assignment, CUDA, m) {
     m.impl("jonker_dense_batch", &jonker_dense_batch_cuda);
+    m.impl("jonker_dense_batch_unpacked", &jonker_dense_batch_unpacked_cuda);
 }
