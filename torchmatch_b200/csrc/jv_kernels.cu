@@ -44,7 +44,7 @@ constexpr uint32_t kWaitLimit = 1u << 26;  // bounded mbarrier wait
 // Optional per-phase cycle counters (build with -DTMJV_PHASE_CLOCKS; the
 // kernel then adds clock64() deltas into tmjv_phase_cycles[]).
 #ifdef TMJV_PHASE_CLOCKS
-__device__ unsigned long long tmjv_phase_cycles[8];
+__device__ unsigned long long tmjv_phase_cycles[16];
 #define TMJV_T(name) const long long name = clock64()
 #define TMJV_ACC(idx, t0)                                                            \
     do {                                                                             \
@@ -166,6 +166,7 @@ struct WarpShared {
     int16_t *queue;    // free-row queue
     int16_t *order;    // column permutation of the Dijkstra phase
     uint8_t *flag;     // per-row "single" bit / per-column event bits
+    int32_t *evbuf;    // compacted events of one minimum search
     uint64_t *bar;     // mbarrier of the tile copy
     // row cache of the augmenting row reduction (streaming mode only)
     float2 *centry;    // [row][kCache]: {cost value, column as int bits}
@@ -181,7 +182,7 @@ __host__ __device__ inline int slots_for(int K) { return (K + 31) / 32; }
 // Per-warp shared bytes: bookkeeping arrays for KP = 32 * S entries.
 __host__ __device__ inline int book_bytes(int KP, bool cache) {
     int b = KP * 4 /*dist*/ + KP * 4 /*xrow*/ + KP * 2 * 4 /*ycol,pred,queue,order*/ +
-            KP /*flag*/ + 32 /*bar + alignment*/;
+            KP /*flag*/ + KP * 4 /*evbuf*/ + 48 /*bar + alignment*/;
     if (cache) b += KP * kCache * 8 + KP * 4 + KP * 4 + KP + 16;
     return b;
 }
@@ -199,6 +200,7 @@ __device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP,
     w.order = reinterpret_cast<int16_t *>(p); p += KP * 2;
     w.flag = p; p += KP;
     p = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
+    w.evbuf = reinterpret_cast<int32_t *>(p); p += KP * 4;
     w.bar = reinterpret_cast<uint64_t *>(p);
     p += 16;
     w.centry = nullptr; w.cbound = nullptr; w.cflag = nullptr; w.vsh = nullptr;
@@ -737,6 +739,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             if (++iter > icap) { failed = true; break; }
             if (lo == hi) {
                 // -- minimum search with the reference's swap pattern (:27-43)
+                TMJV_T(t_find);
                 __syncwarp();
                 if (lo >= K) { failed = true; break; }
                 ready |= grp;
@@ -777,17 +780,40 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     carry = fminf(carry, __shfl_sync(kFull, incl[s], 31));
                 }
                 mind = carry;
-                int nh = lo + 1;
-                if (lane == 0) {
-#pragma unroll 1
+                // compact the events (position, original column, reset?) in
+                // position order; columns at event positions are untouched
+                // until their own event, so they are read here in parallel
+                {
+                    int base = 0;
+#pragma unroll
                     for (int s = 0; s < S; ++s) {
-                        unsigned m = evm[s];
-                        while (m) {
-                            const int l = __ffs(m) - 1;
-                            m &= m - 1;
-                            const int k = s * 32 + l;
-                            const int16_t e = w.order[k];
-                            if (rsm[s] >> l & 1) {
+                        if (evm[s] >> lane & 1) {
+                            const int k = s * 32 + lane;
+                            const int slot = base + __popc(evm[s] & ((1u << lane) - 1));
+                            w.evbuf[slot] = k | ((int)w.order[k] << 9) |
+                                            ((int)(rsm[s] >> lane & 1) << 18);
+                        }
+                        base += __popc(evm[s]);
+                    }
+                    __syncwarp();
+#ifdef TMJV_PHASE_CLOCKS
+                    if (lane == 0) {
+                        unsigned nr = 0;
+                        for (int s = 0; s < S; ++s) nr += __popc(rsm[s]);
+                        atomicAdd(&tmjv_phase_cycles[8], (unsigned long long)base);
+                        atomicAdd(&tmjv_phase_cycles[9], (unsigned long long)nr);
+                        atomicAdd(&tmjv_phase_cycles[10], 1ull);
+                    }
+#endif
+                    int nh = lo + 1;
+                    if (lane == 0 && base > 0) {
+                        // replay :31-41 over the events only
+                        int ev = w.evbuf[0];
+                        for (int q = 0; q < base; ++q) {
+                            const int evn = q + 1 < base ? w.evbuf[q + 1] : 0;
+                            const int k = ev & 511;
+                            const int16_t e = (int16_t)((ev >> 9) & 511);
+                            if (ev >> 18) {
                                 w.order[k] = w.order[lo];
                                 w.order[lo] = e;
                                 nh = lo + 1;
@@ -796,10 +822,13 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                                 w.order[nh] = e;
                                 ++nh;
                             }
+                            ev = evn;
                         }
                     }
+                    nh = __shfl_sync(kFull, nh, 0);
+                    hi = nh;
                 }
-                hi = __shfl_sync(kFull, nh, 0);
+
                 __syncwarp();
 #pragma unroll
                 for (int s = 0; s < S; ++s)
@@ -813,12 +842,14 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     if (p >= lo && p < hi && w.ycol[w.order[p]] < 0) cand = p;
                 }
                 const int pbest = warp_max_i(cand);
+                TMJV_ACC(6, t_find);
                 if (pbest >= 0) {
                     sink = w.order[pbest];
                     break;
                 }
             }
             // -- relax the rows of the group, in group order (:45-73)
+            TMJV_T(t_relax);
             while (lo != hi) {
                 const int j = w.order[lo];
                 ++lo;
@@ -873,19 +904,29 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     __syncwarp();
                     break;
                 }
-                if (lane == 0) {
-                    int nh = hi;
-#pragma unroll 1
+                {
+                    int base = 0;
+#pragma unroll
                     for (int s = 0; s < S; ++s) {
-                        unsigned m = em[s];
-                        while (m) {
-                            const int l = __ffs(m) - 1;
-                            m &= m - 1;
-                            const int k = s * 32 + l;
-                            const int16_t e = w.order[k];
+                        if (em[s] >> lane & 1) {
+                            const int k = s * 32 + lane;
+                            w.evbuf[base + __popc(em[s] & ((1u << lane) - 1))] =
+                                k | ((int)w.order[k] << 9);
+                        }
+                        base += __popc(em[s]);
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        // replay :64-65 (move to the end of the ready group)
+                        int nh = hi;
+                        int cur = w.evbuf[0];
+                        for (int q = 0; q < base; ++q) {
+                            const int nxt = q + 1 < base ? w.evbuf[q + 1] : 0;
+                            const int k = cur & 511;
                             w.order[k] = w.order[nh];
-                            w.order[nh] = e;
+                            w.order[nh] = (int16_t)((cur >> 9) & 511);
                             ++nh;
+                            cur = nxt;
                         }
                     }
                 }
@@ -894,6 +935,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 todo &= ~ev;
                 __syncwarp();
             }
+            TMJV_ACC(7, t_relax);
         }
         if (failed) break;
         // price update of the settled columns (:117-119)
@@ -1348,8 +1390,8 @@ int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int
 // Reads and clears the per-phase cycle counters (debug builds only).
 extern "C" int tm_phase_read(unsigned long long *host8) {
     cudaDeviceSynchronize();
-    cudaMemcpyFromSymbol(host8, tmjv::tmjv_phase_cycles, sizeof(unsigned long long) * 8);
-    unsigned long long z[8] = {0};
+    cudaMemcpyFromSymbol(host8, tmjv::tmjv_phase_cycles, sizeof(unsigned long long) * 16);
+    unsigned long long z[16] = {0};
     cudaMemcpyToSymbol(tmjv::tmjv_phase_cycles, z, sizeof(z));
     return 0;
 }
