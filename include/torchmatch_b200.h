@@ -56,9 +56,14 @@ typedef struct tm_jv_stats {
 } tm_jv_stats;
 
 /* Device scratch of one solve (tm_jv_workspace_bytes() bytes).  `ticket`
- * hands out problems to warps; tm_jv_solve_f32 zeroes it and `status` on
- * the stream before each launch.  `status` receives TM_ERR_UNSOLVED (bit
- * OR) if a problem hit a loop bound; that problem's row is all -1. */
+ * hands out problems to warps; the solves zero it and `status` on the
+ * stream before each launch.  `status` collects TM_WS_* bits (bit OR):
+ * a problem that hit a loop bound (its row is all -1), a wait that timed
+ * out, and -- in the asynchronous entry point -- NaN / -inf in the batch. */
+#define TM_WS_NAN       1
+#define TM_WS_NEG_INF   2
+#define TM_WS_UNSOLVED  4
+#define TM_WS_TIMEOUT   8
 typedef struct tm_jv_workspace {
     tm_jv_stats stats;
     unsigned long long ticket;
@@ -150,6 +155,18 @@ typedef struct tm_jv_unpacked {
 int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int M,
                                        const tm_jv_unpacked *u, void *workspace,
                                        tm_stream_t stream);
+
+/* jonker_dense_batch without any host synchronisation, for CUDA graph
+ * capture: the check-mode solve, then a second launch that reads the batch
+ * statistics on the device and, only if the batch holds +inf, computes the
+ * sentinel there and solves again.  Nothing is read back: NaN / -inf are
+ * reported as TM_WS_NAN / TM_WS_NEG_INF in workspace->status (their
+ * problems' rows are -1), not as a return code.  The reference's op is not
+ * capturable (cuda/dispatch.cu:97-106); its docs describe this as the
+ * graph-safe mode (docs/site/content/2.algorithms/1.assignment/
+ * 1.quickstart.md:262-263). */
+int tm_jonker_dense_batch_async_f32(const float *costs, int64_t B, int N, int M,
+                                    int64_t *out, void *workspace, tm_stream_t stream);
 
 /* The cudaError_t of the last TM_ERR_CUDA on this thread. */
 int tm_last_cuda_error(void);

@@ -30,6 +30,8 @@ TORCH_LIB = LIBDIR / "libtmjv_torch.so"
 
 OP = "assignment::jonker_dense_batch"
 SCHEMA = "(Tensor costs) -> Tensor"
+OP_ASYNC = "assignment::jonker_dense_batch_async"
+SCHEMA_ASYNC = "(Tensor costs) -> (Tensor, Tensor)"
 OP_UNPACKED = "assignment::jonker_dense_batch_unpacked"
 SCHEMA_UNPACKED = "(Tensor costs) -> (Tensor, Tensor, Tensor, Tensor)"
 
@@ -60,6 +62,12 @@ def _fake_unpacked(costs: torch.Tensor):
     )
 
 
+def _fake_async(costs: torch.Tensor):
+    torch._check(costs.dim() == 3, lambda: "costs must be 3D (B, N, M)")
+    return (costs.new_empty(costs.size(0), costs.size(1), dtype=torch.long),
+            costs.new_empty(1, dtype=torch.int32))
+
+
 @functools.cache
 def load() -> None:
     """Define the op (if needed), register its fake and load the CUDA impl."""
@@ -67,7 +75,8 @@ def load() -> None:
         raise ImportError(
             f"{TORCH_LIB} is not built; run `python torchmatch_b200/_build.py`"
         )
-    for name, schema, fake in ((OP, SCHEMA, _fake), (OP_UNPACKED, SCHEMA_UNPACKED, _fake_unpacked)):
+    for name, schema, fake in ((OP, SCHEMA, _fake), (OP_UNPACKED, SCHEMA_UNPACKED, _fake_unpacked),
+                               (OP_ASYNC, SCHEMA_ASYNC, _fake_async)):
         if not _has_op(name):
             lib = torch.library.Library("assignment", "FRAGMENT")
             lib.define(name.split("::")[1] + schema)
@@ -96,6 +105,8 @@ def core() -> ctypes.CDLL:
     lib.tm_jonker_dense_batch_f32_noalloc.restype = i32
     lib.tm_jonker_dense_batch_unpacked_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
     lib.tm_jonker_dense_batch_unpacked_f32.restype = i32
+    lib.tm_jonker_dense_batch_async_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
+    lib.tm_jonker_dense_batch_async_f32.restype = i32
     lib.tm_status_string.restype = ctypes.c_char_p
     lib.tm_status_string.argtypes = [i32]
     for name in ("tm_jv_stats_f32", "tm_jv_sentinel", "tm_jv_solve_f32",
@@ -115,6 +126,7 @@ EXPORTED = (
     "tm_jonker_dense_batch_f32",
     "tm_jonker_dense_batch_f32_noalloc",
     "tm_jonker_dense_batch_unpacked_f32",
+    "tm_jonker_dense_batch_async_f32",
     "tm_last_cuda_error",
     "tm_status_string",
 )

@@ -32,6 +32,8 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "torchmatch_b200.h"
 
 namespace tmjv {
@@ -72,6 +74,8 @@ struct Params {
     int64_t *uuc;                // (B, M) unmatched columns
     int64_t *unm;                // (B,) number of matches
     int check;                   // check mode: classify cells, bail on non-finite
+    int gated;                   // run only if *stats shows +inf and no NaN / -inf;
+                                 // the sentinel is then computed on the device
     int warp_bytes;      // shared-memory bytes per warp
     int tile_floats;     // floats reserved for the staged tile (TILE mode)
     int bulk_ok;         // tile base and size are 16-byte multiples
@@ -961,7 +965,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     // ---- output (cpu/ops.cpp:274-283) ------------------------------------
     __syncwarp();
     emit_result(P, w, lane, b, N, M, !failed);
-    if (failed && lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_ERR_UNSOLVED);
+    if (failed && lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_WS_UNSOLVED);
 }
 
 // --------------------------------------------------------- TMA primitives
@@ -1003,9 +1007,28 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
 
 // ------------------------------------------------------------------ kernel
 template <int S, int VEC, bool TILE, bool FULL>
-__global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ? 1 : 4) jv_batch_kernel(const Params P) {
+__global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ? 1 : 4) jv_batch_kernel(const Params P0) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
+    Params P = P0;
+    if (P.gated) {
+        // second launch of the asynchronous path: the statistics of the
+        // check-mode pass decide on the device whether a sentinel solve is
+        // needed (cuda_common.cuh:245-254 without the host round trip)
+        const uint32_t fl = *reinterpret_cast<volatile const uint32_t *>(&P.stats->flags);
+        const uint32_t mk = *reinterpret_cast<volatile const uint32_t *>(&P.stats->max_key);
+        if (blockIdx.x == 0 && threadIdx.x == 0) {
+            int st = 0;
+            if (fl & TM_STAT_NAN) st |= TM_WS_NAN;
+            if (fl & TM_STAT_NEG_INF) st |= TM_WS_NEG_INF;
+            if (st) atomicOr(P.status, st);
+        }
+        if (!(fl & TM_STAT_POS_INF) || (fl & (TM_STAT_NAN | TM_STAT_NEG_INF))) return;
+        P.sentinel = (fl & TM_STAT_FINITE)
+                         ? __fmul_rn(__fadd_rn(key_to_float(mk), 1.0f), (float)(P.K + 1))
+                         : 1.0f;
+        P.sanitize = 1;
+    }
     const int warp = threadIdx.x >> 5;
     const int wpb = blockDim.x >> 5;
     WarpShared w = carve(smem_raw + (size_t)warp * P.warp_bytes, TILE ? P.tile_floats : 0, 32 * S,
@@ -1042,7 +1065,7 @@ __global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ?
                 for (int64_t k = lane; k < per; k += 32) w.tile[k] = __ldg(g + k);
             }
             if (!__all_sync(kFull, ok)) {
-                if (lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_ERR_CUDA);
+                if (lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_WS_TIMEOUT);
                 return;
             }
             if (P.sanitize) {
@@ -1104,6 +1127,11 @@ struct StreamDevice {
         cudaGetDevice(&prev);
         dev = prev;
         if (s != nullptr) {
+            // cudaStreamGetDevice is refused while the stream is capturing;
+            // a capturing stream belongs to the current device anyway
+            cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+            if (cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+                return;
             err = cudaStreamGetDevice(s, &dev);
             if (err == cudaSuccess && dev != prev) err = cudaSetDevice(dev);
         }
@@ -1158,11 +1186,31 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     if ((int64_t)wpb > need_warps) wpb = (int)need_warps;
     const int smem = wpb * warp_bytes;
     auto kern = jv_batch_kernel<S, VEC, TILE, FULL>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return cuda_fail(e);
+    // The shared-memory opt-in and the occupancy query run once per device
+    // and launch shape, so a steady-state launch is just the kernel (nothing
+    // that a CUDA graph capture would reject).
+    struct Cached { int smem = -1, threads = -1, per_sm = 0; };
+    static Cached cache[64];
+    static std::mutex mu;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wpb * 32, smem);
-    if (e != cudaSuccess) return cuda_fail(e);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        Cached &c = cache[dev];
+        if (c.smem != smem || c.threads != wpb * 32) {
+            cudaError_t e =
+                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            if (e != cudaSuccess) return cuda_fail(e);
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c.per_sm, kern, wpb * 32, smem);
+            if (e != cudaSuccess) return cuda_fail(e);
+            c.smem = smem;
+            c.threads = wpb * 32;
+        }
+        per_sm = c.per_sm;
+    }
+    cudaError_t e;
     if (per_sm < 1) per_sm = 1;
     int64_t blocks = (P.B + wpb - 1) / wpb;
     const int64_t resident = (int64_t)num_sms() * per_sm;
@@ -1268,7 +1316,8 @@ int tm_jv_sentinel(const tm_jv_stats *st, int K, float *sentinel, int *has_pos_i
 
 static int solve_impl(const float *costs, int64_t B, int N, int M, float sentinel,
                       int has_pos_inf, int check, int64_t *out, void *workspace,
-                      tm_stream_t stream_, const tm_jv_unpacked *u = nullptr) {
+                      tm_stream_t stream_, const tm_jv_unpacked *u = nullptr,
+                      int gated = 0) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
     if (B == 0 || N == 0) return TM_OK;
@@ -1281,9 +1330,12 @@ static int solve_impl(const float *costs, int64_t B, int N, int M, float sentine
     if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
     tm_jv_workspace *ws = reinterpret_cast<tm_jv_workspace *>(workspace);
     // check mode starts the statistics from zero; a plain solve keeps them
+    // check mode starts the statistics and status from zero; the gated
+    // second launch keeps both and only resets the ticket
     void *zero_from = check ? static_cast<void *>(&ws->stats) : static_cast<void *>(&ws->ticket);
     const size_t zero_bytes = check ? sizeof(ws->stats) + sizeof(ws->ticket) + sizeof(ws->status)
-                                    : sizeof(ws->ticket) + sizeof(ws->status);
+                              : gated ? sizeof(ws->ticket)
+                                      : sizeof(ws->ticket) + sizeof(ws->status);
     cudaError_t e = cudaMemsetAsync(zero_from, 0, zero_bytes, stream);
     if (e != cudaSuccess) return tmjv::cuda_fail(e);
     if (M == 0) {
@@ -1303,6 +1355,7 @@ static int solve_impl(const float *costs, int64_t B, int N, int M, float sentine
     P.sentinel = sentinel;
     P.sanitize = (has_pos_inf && !check) ? 1 : 0;
     P.check = check;
+    P.gated = gated;
     P.stats = &ws->stats;
     P.out = out;
     if (u) {
@@ -1357,6 +1410,18 @@ int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64
     return TM_OK;
 }
 
+int tm_jonker_dense_batch_async_f32(const float *costs, int64_t B, int N, int M,
+                                    int64_t *out, void *workspace, tm_stream_t stream_) {
+    if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
+    if (B == 0 || N == 0) return TM_OK;
+    if (!out || !workspace) return TM_ERR_ARG;
+    const int K = N > M ? N : M;
+    if (K > tm_jv_max_k()) return TM_ERR_TOO_LARGE;
+    int rc = solve_impl(costs, B, N, M, 0.0f, 0, 1, out, workspace, stream_);
+    if (rc || M == 0) return rc;
+    return solve_impl(costs, B, N, M, 0.0f, 0, 0, out, workspace, stream_, nullptr, 1);
+}
+
 int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int M,
                                        const tm_jv_unpacked *u, void *workspace,
                                        tm_stream_t stream_) {
@@ -1405,7 +1470,6 @@ extern "C" int tm_phase_read(unsigned long long *host8) {
 // device address once per device.
 static __device__ __align__(256) tm_jv_workspace g_noalloc_workspace;
 
-#include <mutex>
 
 namespace {
 std::mutex g_noalloc_mu;

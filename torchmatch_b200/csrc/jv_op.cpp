@@ -22,6 +22,8 @@
 
 #include <cuda_runtime.h>
 
+#include <cstddef>
+
 #include "torchmatch_b200.h"
 
 namespace {
@@ -138,9 +140,45 @@ jonker_dense_batch_unpacked_cuda(const at::Tensor &costs) {
     return {matches, ur, uc, nm};
 }
 
+// jonker_dense_batch_async: the same mapping without any host
+// synchronisation, so it can be captured in a CUDA graph.  Returns the
+// mapping and a one-element int32 status tensor (TM_WS_* bits: 1 NaN,
+// 2 -inf, 4 a problem hit a loop bound, 8 a wait timed out) that stays on the
+// device; NaN / -inf problems are rows of -1.  No counterpart in the
+// reference, whose op refuses capture (cuda/dispatch.cu:97-106).
+std::tuple<at::Tensor, at::Tensor> jonker_dense_batch_async_cuda(const at::Tensor &costs) {
+    TORCH_CHECK(costs.is_cuda(), "costs must be a CUDA tensor");
+    TORCH_CHECK(costs.dim() == 3, "costs must be 3D (B, N, M), got ", costs.dim());
+    TORCH_CHECK(costs.scalar_type() == at::kFloat || costs.scalar_type() == at::kDouble,
+                "costs must be float32 or float64, got ", costs.scalar_type());
+    const c10::cuda::CUDAGuard guard(costs.device());
+    const int64_t B = costs.size(0), N = costs.size(1), M = costs.size(2);
+    TORCH_CHECK(std::max(N, M) <= tm_jv_max_k(), "Batched JV (CUDA) supports max(N, M) <= ",
+                tm_jv_max_k(), ", got K=", std::max(N, M));
+    at::Tensor scratch = at::zeros({(int64_t)tm_jv_workspace_bytes() / 4},
+                                   costs.options().dtype(at::kInt));
+    at::Tensor status = scratch.narrow(0, offsetof(tm_jv_workspace, status) / 4, 1);
+    at::Tensor out = at::empty({B, N}, costs.options().dtype(at::kLong));
+    if (B == 0 || N == 0) return {out, status.clone()};
+    if (M == 0) {
+        out.fill_(-1);
+        return {out, status.clone()};
+    }
+    const at::Tensor c = costs.to(at::kFloat).contiguous();
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+    const int rc = tm_jonker_dense_batch_async_f32(
+        c.const_data_ptr<float>(), B, static_cast<int>(N), static_cast<int>(M),
+        out.mutable_data_ptr<int64_t>(), scratch.mutable_data_ptr(),
+        reinterpret_cast<tm_stream_t>(stream));
+    TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
+    // a fresh tensor (stream-ordered copy) rather than a view into scratch
+    return {out, status.clone()};
+}
+
 }  // namespace
 
 TORCH_LIBRARY_IMPL(assignment, CUDA, m) {
+    m.impl("jonker_dense_batch_async", &jonker_dense_batch_async_cuda);
     m.impl("jonker_dense_batch", &jonker_dense_batch_cuda);
     m.impl("jonker_dense_batch_unpacked", &jonker_dense_batch_unpacked_cuda);
 }
