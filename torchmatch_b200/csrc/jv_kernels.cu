@@ -536,7 +536,14 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
 #pragma unroll
         for (int s = 0; s < S; ++s) {
             const int r = s * 32 + lane;
-            if (r < K) w.cflag[r] = 0;
+            if (r < K) {
+                // no cache yet: a bound of -inf makes every lookup miss, and
+                // column 0 keeps the (then unused) candidate loads in bounds
+                w.cbound[r] = -__int_as_float(0x7f800000);
+#pragma unroll
+                for (int k = 0; k < kCache; ++k)
+                    w.centry[r * kCache + k] = make_float2(0.0f, __int_as_float(0));
+            }
             if (valid >> s & 1) w.vsh[jj[s]] = v[s];
         }
     }
@@ -554,7 +561,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             float v1, v2, bv;
             int j1, bc;
             bool hit = false;
-            if (use_cache && w.cflag[row]) {
+            if (use_cache) {
                 float cv = __int_as_float(0x7f800000);
                 int cj = 0x7fffffff;
                 if (lane < kCache) {
@@ -603,10 +610,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                         rk[k] = m;
                         jk[k] = jm;
                     }
-                    if (lane == 0) {
-                        w.cbound[row] = rk[kCache];
-                        w.cflag[row] = 1;
-                    }
+                    if (lane == 0) w.cbound[row] = rk[kCache];
                     v1 = rk[0];
                     j1 = jk[0];
                     v2 = rk[1];
