@@ -531,7 +531,11 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     // only wide rows pay for the cache: with K < 192 a miss (row scan + top-5
     // extraction) costs more than the reads it saves (low hit rates on tied
     // or masked costs)
-    const bool use_cache = kCached && K >= 192;
+    // Cached mode: streaming rows with K > 192.  Prices and the row of each
+    // column then live in shared memory only during this phase (lookups are
+    // broadcast loads, updates single stores); the lane registers are
+    // refreshed on misses and at the end of the phase.
+    constexpr bool use_cache = kCached && S >= 7;
     if (use_cache) {
 #pragma unroll
         for (int s = 0; s < S; ++s) {
@@ -578,7 +582,10 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             }
             if (!hit) {
                 load_row<S, VEC, TILE, FULL>(src, row, N, M, lane, sanitize, sentinel, c);
-                if (use_cache) {
+                if constexpr (use_cache) {
+#pragma unroll
+                    for (int t = 0; t < S; ++t)
+                        if (valid >> t & 1) v[t] = w.vsh[jj[t]];
                     // lexicographic top-(kCache+1) by repeated extraction:
                     // ranks 0-1 answer this step, ranks 0..kCache-1 are
                     // cached, rank kCache bounds every uncached column
@@ -645,8 +652,20 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             // the owner lane's price and row of j1 are fetched before the rare
             // LARGE check, which would otherwise sit on the critical path
             int l1 = L::lane_of(j1), s1 = L::slot_of(j1);
-            float vj1 = __shfl_sync(kFull, sel(v, s1), l1);
-            int i0 = __shfl_sync(kFull, seli(yc, s1), l1);
+            float vj1;
+            int i0;
+            if constexpr (use_cache) {
+                vj1 = w.vsh[j1];
+                i0 = w.ycol[j1];
+            } else {
+                if constexpr (use_cache) {
+                    vj1 = w.vsh[j1];
+                    i0 = w.ycol[j1];
+                } else {
+                    vj1 = __shfl_sync(kFull, sel(v, s1), l1);
+                    i0 = __shfl_sync(kFull, seli(yc, s1), l1);
+                }
+            }
             if (__builtin_expect(!(v2 < kBig), 0)) {
                 // a reduced cost at or above LARGE: replay the scalar scan
                 // of :193-210 exactly (its result is not the plain top-2 then)
@@ -673,8 +692,13 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 __syncwarp();
                 l1 = L::lane_of(j1);
                 s1 = L::slot_of(j1);
-                vj1 = __shfl_sync(kFull, sel(v, s1), l1);
-                i0 = __shfl_sync(kFull, seli(yc, s1), l1);
+                if constexpr (use_cache) {
+                    vj1 = w.vsh[j1];
+                    i0 = w.ycol[j1];
+                } else {
+                    vj1 = __shfl_sync(kFull, sel(v, s1), l1);
+                    i0 = __shfl_sync(kFull, seli(yc, s1), l1);
+                }
             }
             const float lowered = vj1 - (v2 - v1);
             const bool lowers = lowered < vj1;
@@ -685,7 +709,8 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 if (j2 == -2) j2 = (int)warp_min_u(bv == v2 ? (unsigned)bc : 0xffffffffu);
                 if (j2 >= 0) {
                     jsel = j2;
-                    i0 = __shfl_sync(kFull, seli(yc, L::slot_of(j2)), L::lane_of(j2));
+                    if constexpr (use_cache) i0 = w.ycol[j2];
+                    else i0 = __shfl_sync(kFull, seli(yc, L::slot_of(j2)), L::lane_of(j2));
                 }
             }
             if (i0 >= 0) {
@@ -695,12 +720,16 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             // branch-free register updates of the owner lanes
             const bool own1 = early && lowers && lane == l1;
             const int ls = L::lane_of(jsel), ss = L::slot_of(jsel);
+            if constexpr (use_cache) {
+                if (early && lowers) w.vsh[j1] = lowered;  // same word from every lane
+                w.ycol[jsel] = (int16_t)row;
+            } else {
 #pragma unroll
-            for (int t = 0; t < S; ++t) {
-                v[t] = (own1 && t == s1) ? lowered : v[t];
-                yc[t] = (lane == ls && t == ss) ? row : yc[t];
+                for (int t = 0; t < S; ++t) {
+                    v[t] = (own1 && t == s1) ? lowered : v[t];
+                    yc[t] = (lane == ls && t == ss) ? row : yc[t];
+                }
             }
-            if (use_cache && own1) w.vsh[j1] = lowered;
             // every lane stores the same word: no divergent branch
             w.xrow[row] = jsel;
             if (push_back) w.queue[kept] = (int16_t)i0;
@@ -716,10 +745,20 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         nfree = kept;
         __syncwarp();
     }
-    // the Dijkstra phase reads y through shared memory
+    // the Dijkstra phase reads y through shared memory (and, in cached mode,
+    // finds the prices there)
+    if constexpr (use_cache) {
 #pragma unroll
-    for (int s = 0; s < S; ++s)
-        if (valid >> s & 1) w.ycol[jj[s]] = (int16_t)yc[s];
+        for (int s = 0; s < S; ++s)
+            if (valid >> s & 1) {
+                v[s] = w.vsh[jj[s]];
+                yc[s] = w.ycol[jj[s]];
+            }
+    } else {
+#pragma unroll
+        for (int s = 0; s < S; ++s)
+            if (valid >> s & 1) w.ycol[jj[s]] = (int16_t)yc[s];
+    }
     __syncwarp();
 
     TMJV_ACC(3, t_arr);
