@@ -74,6 +74,7 @@ struct Params {
     int64_t *uuc;                // (B, M) unmatched columns
     int64_t *unm;                // (B,) number of matches
     int check;                   // check mode: classify cells, bail on non-finite
+    int l2_prefetch;             // streaming mode: prefetch each claimed problem into L2
     int gated;                   // run only if *stats shows +inf and no NaN / -inf;
                                  // the sentinel is then computed on the device
     int warp_bytes;      // shared-memory bytes per warp
@@ -1118,6 +1119,10 @@ __global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ?
             __syncwarp();
             src = w.tile;
             if (P.bulk_ok && lane == 0 && nb < P.B) prefetch_l2(P.costs + nb * per, tile_bytes);
+        } else {
+            // streaming mode: pull the claimed problem's block into L2 up front
+            // (when it is small enough for the resident set to stay there)
+            if (P.l2_prefetch && P.bulk_ok && lane == 0) prefetch_l2(g, tile_bytes);
         }
         TMJV_ACC(0, t_load);
         solve_problem<S, VEC, TILE, FULL>(src, P, w, lane, b);
@@ -1201,6 +1206,17 @@ constexpr int kSmemLimit = 227 * 1024;
 
 // Minimum number of resident warps per SM for the shared-memory tile mode
 // (TM_JV_TILE_MIN_WARPS overrides the default of 4; 0 disables the mode).
+// Prefetch of each claimed problem into L2 in streaming mode
+// (TM_JV_L2_PREFETCH=0 disables it).
+static int l2_prefetch_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("TM_JV_L2_PREFETCH");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v;
+}
+
 static int tile_min_warps() {
     static int v = -1;
     if (v < 0) {
@@ -1399,6 +1415,7 @@ static int solve_impl(const float *costs, int64_t B, int N, int M, float sentine
     P.sanitize = (has_pos_inf && !check) ? 1 : 0;
     P.check = check;
     P.gated = gated;
+    P.l2_prefetch = tmjv::l2_prefetch_enabled();
     P.stats = &ws->stats;
     P.out = out;
     if (u) {
