@@ -575,10 +575,15 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     cv = e.x - w.vsh[cj];
                 }
                 v1 = warp_min_f(cv);
-                j1 = (int)warp_min_u(cv == v1 ? (unsigned)cj : 0xffffffffu);
+                const bool at1 = cv == v1;
+                const unsigned ties = __ballot_sync(kFull, at1);
+                j1 = (int)warp_min_u(at1 ? (unsigned)cj : 0xffffffffu);
+                // one candidate per lane: with two candidates at v1 the second
+                // best is v1 itself, otherwise the best of the other lanes
+                const float v2b = warp_min_f(at1 ? __int_as_float(0x7f800000) : cv);
+                v2 = __popc(ties) > 1 ? v1 : v2b;
                 bv = cj == j1 ? __int_as_float(0x7f800000) : cv;
                 bc = cj;
-                v2 = warp_min_f(bv);
                 hit = v2 < w.cbound[row] && v2 < kBig;
             }
             if (!hit) {
@@ -737,7 +742,9 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             kept += push_back;
             head -= push_front;
             row = push_front ? i0 : queued;
-            if (use_cache) __syncwarp();  // cache / price mirror writes visible
+            // a hit only stores words that every lane writes itself; a miss
+            // wrote per-lane cache entries that other lanes read later
+            if (use_cache && !hit) __syncwarp();
         }
 #ifdef TMJV_PHASE_CLOCKS
         if (lane == 0) atomicAdd(&tmjv_phase_cycles[5], (unsigned long long)visits);
