@@ -168,6 +168,19 @@ int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int
 int tm_jonker_dense_batch_async_f32(const float *costs, int64_t B, int N, int M,
                                     int64_t *out, void *workspace, tm_stream_t stream);
 
+/* jonker_compact_batch and jonker_compact_batch_unpacked: the same batch
+ * driver over the reference's "compact" solver variant
+ * (cpu/jonker_compact_core.h:51-252; CPU-only in the reference), which
+ * differs from the dense one in its column-reduction seed, its FLT_MAX
+ * initial values, the missing visit bound of the row reduction, the first
+ * (not last) free column of a tie group and the rounding of its price
+ * update.  Same arguments as the dense entry points. */
+int tm_jonker_compact_batch_f32(const float *costs, int64_t B, int N, int M, int64_t *out,
+                                void *workspace, tm_stream_t stream);
+int tm_jonker_compact_batch_unpacked_f32(const float *costs, int64_t B, int N, int M,
+                                         const tm_jv_unpacked *u, void *workspace,
+                                         tm_stream_t stream);
+
 /* The cudaError_t of the last TM_ERR_CUDA on this thread. */
 int tm_last_cuda_error(void);
 

@@ -74,6 +74,16 @@ def jonker_dense_batch(costs, threads: int = 0) -> np.ndarray:
     return _call(LIB, "tmo_jonker_dense_batch_f32", costs, threads)
 
 
+def jonker_compact_batch(costs, threads: int = 0) -> np.ndarray:
+    """Oracle restatement of jonker_compact_batch (cpu/jonker_compact_core.h)."""
+    return _call(LIB, "tmo_jonker_compact_batch_f32", costs, threads)
+
+
+def reference_jonker_compact_batch(costs, threads: int = 0) -> np.ndarray:
+    """The reference's compact solver behind the same batch driver."""
+    return _call(REF_LIB, "tmref_jonker_compact_batch_f32", costs, threads)
+
+
 def reference_available() -> bool:
     return REF_LIB.exists()
 

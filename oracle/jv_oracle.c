@@ -10,6 +10,12 @@
  *   - cpu/ops.cpp:176-289   solve_batch: pad each problem to K x K (pad cells
  *                           0, non-finite cells -> sentinel), solve, map
  *                           columns >= M to -1
+ *   - cpu/jonker_compact_core.h:51-252  the "compact" variant of the same
+ *                           phases (jonker_compact_batch), selected by
+ *                           jv_work.compact: column minima seeded from row 0,
+ *                           FLT_MAX instead of LARGE, no visit bound in the
+ *                           row reduction, the FIRST free column of a tie
+ *                           group, and the price update (v + d) - min
  *   - cpu/jonker_dense_flat.h:124-274  the four LAPJV phases in fp32:
  *       column reduction + reduction transfer  (ccrrt_dense  :124-176)
  *       augmenting row reduction, run twice    (carr_dense   :178-235)
@@ -51,6 +57,7 @@ typedef struct {
 /* Per-problem working arrays, one set per thread. */
 typedef struct {
     int n;
+    int compact;          /* jonker_compact_core.h semantics */
     int32_t *row_of_col;  /* y */
     int32_t *col_of_row;  /* x */
     int32_t *queue;       /* free rows */
@@ -89,12 +96,12 @@ static int phase_reduce(const float *c, jv_work *w) {
     float *v = w->price;
     for (int k = 0; k < n; ++k) {
         x[k] = -1;
-        v[k] = TMO_BIG;
+        v[k] = w->compact ? c[k] : TMO_BIG;  /* compact_core.h:79-80 */
         y[k] = 0;
         w->single[k] = 1;
     }
     /* cheapest row of every column; the first such row wins (strict <) */
-    for (int i = 0; i < n; ++i) {
+    for (int i = w->compact ? 1 : 0; i < n; ++i) {
         const float *ci = c + (size_t)i * n;
         for (int j = 0; j < n; ++j)
             if (ci[j] < v[j]) {
@@ -123,7 +130,7 @@ static int phase_reduce(const float *c, jv_work *w) {
             continue;
         const float *ci = c + (size_t)i * n;
         const int own = x[i];
-        float best = TMO_BIG;
+        float best = w->compact ? FLT_MAX : TMO_BIG;  /* compact_core.h:104 */
         for (int j = 0; j < n; ++j) {
             if (j == own)
                 continue;
@@ -150,7 +157,7 @@ static int phase_arr(const float *c, jv_work *w, int nfree) {
         const float *ci = c + (size_t)row * n;
         /* two smallest reduced costs, first index wins ties */
         int a = 0, b = -1;
-        float va = ci[0] - v[0], vb = TMO_BIG;
+        float va = ci[0] - v[0], vb = w->compact ? FLT_MAX : TMO_BIG;
         for (int j = 1; j < n; ++j) {
             const float r = ci[j] - v[j];
             if (r < vb) {
@@ -168,10 +175,11 @@ static int phase_arr(const float *c, jv_work *w, int nfree) {
         int owner = y[a];
         const float lowered = v[a] - (vb - va);
         const int lowers = lowered < v[a];
-        if (visits < head * (unsigned)n) {
+        /* the compact variant has no visit bound (compact_core.h:145-169) */
+        if (w->compact || visits < head * (unsigned)n) {
             if (lowers) {
                 v[a] = lowered;
-            } else if (owner >= 0 && b >= 0) {
+            } else if (owner >= 0 && (b >= 0 || w->compact)) {
                 a = b;
                 owner = y[b];
             }
@@ -263,15 +271,22 @@ static int shortest_path(int n, const float *c, int start, jv_work *w) {
             settled = lo;
             hi = take_minimum(n, lo, d, order);
             for (int k = lo; k < hi; ++k)
-                if (y[order[k]] < 0)
+                if (y[order[k]] < 0) {
                     sink = order[k];   /* last free column of the group */
+                    if (w->compact)
+                        break;         /* compact: the first (:195-201) */
+                }
         }
         if (sink == -1)
             sink = relax_group(n, c, &lo, &hi, w);
     }
     const float best = d[order[lo]];
-    for (int k = 0; k < settled; ++k)
-        v[order[k]] += d[order[k]] - best;
+    for (int k = 0; k < settled; ++k) {
+        if (w->compact)
+            v[order[k]] = v[order[k]] + d[order[k]] - best;  /* :232-235 */
+        else
+            v[order[k]] += d[order[k]] - best;
+    }
     return sink;
 }
 
@@ -290,7 +305,7 @@ static void phase_augment(const float *c, jv_work *w, int nfree) {
             const int prev = x[i];
             x[i] = j;
             j = prev;
-            if (++steps >= n)
+            if (++steps >= n && !w->compact)
                 break;
         } while (i != start);
     }
@@ -338,8 +353,8 @@ float tmo_sentinel_f32(const tmo_stats *s, int K) {
  * costs: (B, N, M) contiguous fp32; out: (B, N) int64.
  * Returns 0, 1 if the batch holds a NaN, 2 if it holds -inf, 3 on an
  * allocation failure.  nthreads <= 0 uses the OpenMP default. */
-int tmo_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M,
-                               int64_t *out, int nthreads) {
+static int batch_driver(const float *costs, int64_t B, int N, int M, int64_t *out,
+                        int nthreads, int compact) {
     if (B <= 0 || N <= 0 || M <= 0) {
         for (int64_t k = 0; k < (B > 0 ? B : 0) * (N > 0 ? N : 0); ++k)
             out[k] = -1;
@@ -362,7 +377,9 @@ int tmo_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M,
     {
         jv_work w;
         float *pad = (float *)malloc(sizeof(float) * (size_t)K * K);
-        if (!work_init(&w, K) || !pad) {
+        const int ok = work_init(&w, K);
+        w.compact = compact;
+        if (!ok || !pad) {
             failed = 1;
         } else {
 #ifdef _OPENMP
@@ -392,4 +409,16 @@ int tmo_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M,
         free(pad);
     }
     return failed ? 3 : 0;
+}
+
+/* jonker_dense_batch (cpu/ops.cpp:176-289 with jonker_dense_flat.h). */
+int tmo_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M,
+                               int64_t *out, int nthreads) {
+    return batch_driver(costs, B, N, M, out, nthreads, 0);
+}
+
+/* jonker_compact_batch (the same driver with jonker_compact_core.h). */
+int tmo_jonker_compact_batch_f32(const float *costs, int64_t B, int N, int M,
+                                 int64_t *out, int nthreads) {
+    return batch_driver(costs, B, N, M, out, nthreads, 1);
 }

@@ -4,7 +4,8 @@
 // so the tests can pin oracle/jv_oracle.c against the reference itself and
 // bench.py can time the reference's CPU solver as its baseline arm.
 //
-// The batch driver below restates cpu/ops.cpp:176-289 (float32 branch):
+// The batch driver below restates cpu/ops.cpp:176-289 (float32 branch), used
+// for both jonker_dense_batch and jonker_compact_batch:
 // batch-global sentinel, pad to K x K, one square solve per problem,
 // columns >= M mapped to -1.  The square solve is the reference's
 // jonker_dense_solve_square_f32 (jonker_dense_core.cpp:57-60).
@@ -14,13 +15,17 @@
 #include <vector>
 #include <omp.h>
 
+#include "jonker_compact_core.h"  // header-only, from the reference tree
+
 namespace match_jonker::detail {
 int jonker_dense_solve_square_f32(const float *cost_flat, int n, int64_t *row_to_col,
                                   int64_t *col_to_row);
 }
 
-extern "C" int tmref_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M,
-                                            int64_t *out, int nthreads) {
+using SquareFn = int (*)(const float *, int, int64_t *, int64_t *);
+
+static int batch(const float *costs, int64_t B, int N, int M, int64_t *out, int nthreads,
+                 SquareFn solve) {
     if (B <= 0 || N <= 0 || M <= 0) {
         for (int64_t k = 0; k < (B > 0 ? B : 0) * (N > 0 ? N : 0); ++k) out[k] = -1;
         return 0;
@@ -56,8 +61,7 @@ extern "C" int tmref_jonker_dense_batch_f32(const float *costs, int64_t B, int N
                     }
                     pad[(size_t)i * K + j] = val;
                 }
-            const int rc = match_jonker::detail::jonker_dense_solve_square_f32(
-                pad.data(), K, r2c.data(), c2r.data());
+            const int rc = solve(pad.data(), K, r2c.data(), c2r.data());
             int64_t *ob = out + b * (int64_t)N;
             for (int i = 0; i < N; ++i) {
                 const int64_t j = r2c[i];
@@ -67,4 +71,18 @@ extern "C" int tmref_jonker_dense_batch_f32(const float *costs, int64_t B, int N
         }
     }
     return failed ? 3 : 0;
+}
+
+extern "C" int tmref_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M,
+                                            int64_t *out, int nthreads) {
+    return batch(costs, B, N, M, out, nthreads,
+                 &match_jonker::detail::jonker_dense_solve_square_f32);
+}
+
+// jonker_compact_batch: the same driver over the reference's compact solver
+// (jonker_compact_core.h:276-300).
+extern "C" int tmref_jonker_compact_batch_f32(const float *costs, int64_t B, int N, int M,
+                                              int64_t *out, int nthreads) {
+    return batch(costs, B, N, M, out, nthreads,
+                 &match_jonker::detail::jonker_compact_solve_square_f32);
 }

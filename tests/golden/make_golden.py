@@ -1,8 +1,9 @@
 """Regenerates tests/golden/golden.npz from the reference itself.
 
-Runs the reference's own ``torch.ops.assignment.jonker_dense_batch`` (CPU
-backend of tue-p8n/torchmatch, cpu/ops.cpp:176-289) on every recipe of
-cases.py and stores its int64 outputs (as int16) plus the input digests.
+Runs the reference's own ``torch.ops.assignment.jonker_dense_batch`` and
+``jonker_compact_batch`` (CPU backend of tue-p8n/torchmatch, cpu/ops.cpp:176-289)
+on every recipe of cases.py and stores their int64 outputs (as int16, the
+compact ones under ``compact__<case>``) plus the input digests.
 Needs the reference source tree; run in a container that has it:
 
     REF=/path/to/torchmatch/sources TORCHMATCH_FORCE_JIT=1 \
@@ -30,11 +31,13 @@ from cases import CASES, digest  # noqa: E402
 
 def main() -> None:
     op = torch.ops.assignment.jonker_dense_batch
+    op_compact = torch.ops.assignment.jonker_compact_batch
     arrays, meta = {}, {}
     for name, make in CASES.items():
         x = make()
         out = op(x)
         arrays[name] = out.numpy().astype(np.int16)
+        arrays["compact__" + name] = op_compact(x).numpy().astype(np.int16)
         meta[name] = {"shape": list(x.shape), "sha256": digest(x)}
         print(name, tuple(x.shape))
     np.savez_compressed(HERE / "golden.npz", **arrays)

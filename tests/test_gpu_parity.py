@@ -273,3 +273,27 @@ def test_unpacked_opcheck_and_solve_route():
     packed = solve(x).cpu().numpy()
     for g, w in zip(native, _unpack_like_reference(packed, 17)):
         np.testing.assert_array_equal(g.cpu().numpy(), w)
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_compact_golden(name, golden):
+    outs, _ = golden
+    got = torch.ops.assignment.jonker_compact_batch(CASES[name]().cuda()).cpu().numpy()
+    np.testing.assert_array_equal(got, outs["compact__" + name])
+
+
+@pytest.mark.parametrize("make", [lambda: config2(2048), lambda: config3(1024),
+                                  lambda: config4(1024), lambda: config5_chunk(256, 7)])
+def test_compact_matches_oracle(make, oracle_mod):
+    x = make().contiguous()
+    got = torch.ops.assignment.jonker_compact_batch(x.cuda()).cpu().numpy()
+    np.testing.assert_array_equal(got, oracle_mod.jonker_compact_batch(x.numpy()))
+
+
+def test_compact_unpacked_layout(golden):
+    outs, _ = golden
+    x = CASES["config4_b256"]()
+    got = torch.ops.assignment.jonker_compact_batch_unpacked(x.cuda())
+    want = _unpack_like_reference(outs["compact__config4_b256"], x.shape[2])
+    for g, w in zip(got, want):
+        np.testing.assert_array_equal(g.cpu().numpy(), w)

@@ -69,3 +69,20 @@ def test_oracle_is_a_valid_optimum(oracle_mod):
         opt = x[b].astype(np.float64)[r, c].sum()
         got = x[b].astype(np.float64)[np.arange(64), out[b]].sum()
         assert abs(got - opt) < 1e-5
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_compact_oracle_matches_golden(name, golden, oracle_mod):
+    outs, _ = golden
+    got = oracle_mod.jonker_compact_batch(CASES[name]().numpy())
+    np.testing.assert_array_equal(got, outs["compact__" + name])
+
+
+@pytest.mark.parametrize("name", ["config2", "config3", "config4", "config5", "ties"])
+def test_compact_oracle_matches_compiled_reference(name, oracle_mod):
+    if not oracle_mod.reference_available():
+        pytest.skip("oracle/_ref not built (reference tree absent)")
+    x = _ref_cases()[name].numpy()
+    np.testing.assert_array_equal(
+        oracle_mod.jonker_compact_batch(x), oracle_mod.reference_jonker_compact_batch(x)
+    )

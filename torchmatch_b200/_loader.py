@@ -33,6 +33,8 @@ SCHEMA = "(Tensor costs) -> Tensor"
 OP_ASYNC = "assignment::jonker_dense_batch_async"
 SCHEMA_ASYNC = "(Tensor costs) -> (Tensor, Tensor)"
 OP_UNPACKED = "assignment::jonker_dense_batch_unpacked"
+OP_COMPACT = "assignment::jonker_compact_batch"
+OP_COMPACT_UNPACKED = "assignment::jonker_compact_batch_unpacked"
 SCHEMA_UNPACKED = "(Tensor costs) -> (Tensor, Tensor, Tensor, Tensor)"
 
 _LIB_HANDLES: list[object] = []
@@ -76,7 +78,9 @@ def load() -> None:
             f"{TORCH_LIB} is not built; run `python torchmatch_b200/_build.py`"
         )
     for name, schema, fake in ((OP, SCHEMA, _fake), (OP_UNPACKED, SCHEMA_UNPACKED, _fake_unpacked),
-                               (OP_ASYNC, SCHEMA_ASYNC, _fake_async)):
+                               (OP_ASYNC, SCHEMA_ASYNC, _fake_async),
+                               (OP_COMPACT, SCHEMA, _fake),
+                               (OP_COMPACT_UNPACKED, SCHEMA_UNPACKED, _fake_unpacked)):
         if not _has_op(name):
             lib = torch.library.Library("assignment", "FRAGMENT")
             lib.define(name.split("::")[1] + schema)
@@ -107,6 +111,10 @@ def core() -> ctypes.CDLL:
     lib.tm_jonker_dense_batch_unpacked_f32.restype = i32
     lib.tm_jonker_dense_batch_async_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
     lib.tm_jonker_dense_batch_async_f32.restype = i32
+    lib.tm_jonker_compact_batch_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
+    lib.tm_jonker_compact_batch_f32.restype = i32
+    lib.tm_jonker_compact_batch_unpacked_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
+    lib.tm_jonker_compact_batch_unpacked_f32.restype = i32
     lib.tm_status_string.restype = ctypes.c_char_p
     lib.tm_status_string.argtypes = [i32]
     for name in ("tm_jv_stats_f32", "tm_jv_sentinel", "tm_jv_solve_f32",
@@ -127,6 +135,8 @@ EXPORTED = (
     "tm_jonker_dense_batch_f32_noalloc",
     "tm_jonker_dense_batch_unpacked_f32",
     "tm_jonker_dense_batch_async_f32",
+    "tm_jonker_compact_batch_f32",
+    "tm_jonker_compact_batch_unpacked_f32",
     "tm_last_cuda_error",
     "tm_status_string",
 )

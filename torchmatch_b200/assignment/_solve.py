@@ -47,9 +47,9 @@ _OPS = types.SimpleNamespace(
     jonker_scalar=_op("jonker_scalar"),
     jonker_dense=_op("jonker_dense"),
     jonker_compact=_op("jonker_compact"),
-    jonker_compact_batch=_op("jonker_compact_batch"),
+    jonker_compact_batch=torch.ops.assignment.jonker_compact_batch,
     jonker_dense_batch_unpacked=torch.ops.assignment.jonker_dense_batch_unpacked,
-    jonker_compact_batch_unpacked=_op("jonker_compact_batch_unpacked"),
+    jonker_compact_batch_unpacked=torch.ops.assignment.jonker_compact_batch_unpacked,
     munkres=_op("munkres"),
     lawler=_op("lawler"),
     greedy=_op("greedy"),

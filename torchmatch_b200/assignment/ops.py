@@ -16,11 +16,14 @@ jonker_dense_batch_unpacked = _OPS.jonker_dense_batch_unpacked
 # graph-capturable variant: (mapping, device status) without a host sync
 jonker_dense_batch_async = _OPS.jonker_dense_batch_async
 
-__all__ = ["jonker_dense_batch", "jonker_dense_batch_async", "jonker_dense_batch_unpacked"]
+jonker_compact_batch = _OPS.jonker_compact_batch
+jonker_compact_batch_unpacked = _OPS.jonker_compact_batch_unpacked
+
+__all__ = ["jonker_compact_batch", "jonker_compact_batch_unpacked", "jonker_dense_batch",
+           "jonker_dense_batch_async", "jonker_dense_batch_unpacked"]
 
 for _name in (
-    "jonker_scalar", "jonker_dense", "jonker_compact", "jonker_compact_batch",
-    "jonker_compact_batch_unpacked",
+    "jonker_scalar", "jonker_dense", "jonker_compact",
     "munkres", "hybrid", "lawler", "greedy",
 ):
     if hasattr(_OPS, _name):

@@ -29,6 +29,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <math.h>
+#include <float.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -74,6 +75,7 @@ struct Params {
     int64_t *uuc;                // (B, M) unmatched columns
     int64_t *unm;                // (B,) number of matches
     int check;                   // check mode: classify cells, bail on non-finite
+    int compact;                 // jonker_compact_batch semantics (compact_core.h)
     int l2_prefetch;             // streaming mode: prefetch each claimed problem into L2
     int gated;                   // run only if *stats shows +inf and no NaN / -inf;
                                  // the sentinel is then computed on the device
@@ -392,7 +394,10 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     int ymin[S];
     uint32_t chk_fl = 0, chk_mk = 0;  // check mode: cell classes, max finite key
 #pragma unroll
-    for (int s = 0; s < S; ++s) { v[s] = kBig; ymin[s] = 0; }
+    // compact variant (jonker_compact_core.h:78-86) seeds each column with
+    // row 0; a +inf seed with the same strict < gives exactly that
+    const float seed = P.compact ? __int_as_float(0x7f800000) : kBig;
+    for (int s = 0; s < S; ++s) { v[s] = seed; ymin[s] = 0; }
     {
         const int nreal = N < K ? N : K;
         int i = 0;
@@ -505,7 +510,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             m &= m - 1;
             const int own = w.xrow[i];
             load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c);
-            float loc = kBig;
+            float loc = P.compact ? FLT_MAX : kBig;  // compact_core.h:104
 #pragma unroll
             for (int t = 0; t < S; ++t)
                 if (jj[t] != own) loc = fminf(loc, c[t] - v[t]);
@@ -553,10 +558,16 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         }
     }
     __syncwarp();
+    // the two-min scan's initial second value: LARGE (jonker_dense_flat.h:196)
+    // or FLT_MAX (compact_core.h:26); below it the scan is the plain top-2
+    const float big2 = P.compact ? FLT_MAX : kBig;
     for (int pass = 0; pass < 2 && nfree > 0 && !failed; ++pass) {
         unsigned head = 0, visits = 0;
         int kept = 0;
-        const unsigned cap = (unsigned)K * (unsigned)K + 2u * K + 8u;
+        // the dense rule `rr_cnt < current * n` bounds the visits by K*K + K;
+        // the compact variant has no such rule, so its bound is a safety net
+        const unsigned cap = P.compact ? 64u * (unsigned)K * (unsigned)K + 4096u
+                                       : (unsigned)K * (unsigned)K + 2u * K + 8u;
         int row = w.queue[0];
         while (head < (unsigned)nfree && visits < cap) {
             ++visits;
@@ -584,7 +595,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 v2 = __popc(ties) > 1 ? v1 : v2b;
                 bv = cj == j1 ? __int_as_float(0x7f800000) : cv;
                 bc = cj;
-                hit = v2 < w.cbound[row] && v2 < kBig;
+                hit = v2 < w.cbound[row] && v2 < big2;
             }
             if (!hit) {
                 load_row<S, VEC, TILE, FULL>(src, row, N, M, lane, sanitize, sentinel, c);
@@ -672,7 +683,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     i0 = __shfl_sync(kFull, seli(yc, s1), l1);
                 }
             }
-            if (__builtin_expect(!(v2 < kBig), 0)) {
+            if (__builtin_expect(!(v2 < big2), 0)) {
                 // a reduced cost at or above LARGE: replay the scalar scan
                 // of :193-210 exactly (its result is not the plain top-2 then)
 #pragma unroll
@@ -680,7 +691,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     if (valid >> t & 1) w.dist[jj[t]] = c[t] - v[t];
                 __syncwarp();
                 int ja = 0, jb = -1;
-                float va = 0.0f, vb = kBig;
+                float va = 0.0f, vb = big2;
                 if (lane == 0) {
                     va = w.dist[0];
                     for (int j = 1; j < K; ++j) {
@@ -709,7 +720,8 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             const float lowered = vj1 - (v2 - v1);
             const bool lowers = lowered < vj1;
             int jsel = j1;
-            const bool early = visits < head * (unsigned)K;  // rr_cnt < current * n
+            // rr_cnt < current * n (absent from the compact variant)
+            const bool early = P.compact || visits < head * (unsigned)K;
             bool push_front = false, push_back = false;
             if (early && !lowers && i0 >= 0) {
                 if (j2 == -2) j2 = (int)warp_min_u(bv == v2 ? (unsigned)bc : 0xffffffffu);
@@ -889,14 +901,24 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 for (int s = 0; s < S; ++s)
                     if ((todo >> s & 1) && d[s] == mind) grp |= 1u << s;
                 todo &= ~grp;
-                // last free column of the group, in group order (:107-111)
-                int cand = -1;
+                // last free column of the group, in group order (:107-111);
+                // the compact variant takes the first (compact_core.h:195-201)
+                int cand = -1, candf = 0x7fffffff;
 #pragma unroll
                 for (int s = 0; s < S; ++s) {
                     const int p = s * 32 + lane;
-                    if (p >= lo && p < hi && w.ycol[w.order[p]] < 0) cand = p;
+                    if (p >= lo && p < hi && w.ycol[w.order[p]] < 0) {
+                        cand = p;
+                        candf = min(candf, p);
+                    }
                 }
-                const int pbest = warp_max_i(cand);
+                int pbest;
+                if (P.compact) {
+                    pbest = (int)warp_min_u((unsigned)candf);
+                    if (pbest == 0x7fffffff) pbest = -1;
+                } else {
+                    pbest = warp_max_i(cand);
+                }
                 TMJV_ACC(6, t_find);
                 if (pbest >= 0) {
                     sink = w.order[pbest];
@@ -996,7 +1018,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         // price update of the settled columns (:117-119)
 #pragma unroll
         for (int s = 0; s < S; ++s)
-            if (ready >> s & 1) v[s] += d[s] - mind;
+            if (ready >> s & 1) v[s] = P.compact ? (v[s] + d[s]) - mind : v[s] + (d[s] - mind);
         // augmentation along the predecessor chain (:244-255)
         if (lane == 0) {
             int j = sink, steps = 0, i;
@@ -1383,7 +1405,7 @@ int tm_jv_sentinel(const tm_jv_stats *st, int K, float *sentinel, int *has_pos_i
 static int solve_impl(const float *costs, int64_t B, int N, int M, float sentinel,
                       int has_pos_inf, int check, int64_t *out, void *workspace,
                       tm_stream_t stream_, const tm_jv_unpacked *u = nullptr,
-                      int gated = 0) {
+                      int gated = 0, int compact = 0) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
     if (B == 0 || N == 0) return TM_OK;
@@ -1421,6 +1443,7 @@ static int solve_impl(const float *costs, int64_t B, int N, int M, float sentine
     P.sentinel = sentinel;
     P.sanitize = (has_pos_inf && !check) ? 1 : 0;
     P.check = check;
+    P.compact = compact;
     P.gated = gated;
     P.l2_prefetch = tmjv::l2_prefetch_enabled();
     P.stats = &ws->stats;
@@ -1448,19 +1471,19 @@ int tm_jv_solve_checked_f32(const float *costs, int64_t B, int N, int M, int64_t
 
 size_t tm_jv_workspace_bytes(void) { return sizeof(tm_jv_workspace); }
 
-int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64_t *out,
-                              void *workspace, tm_stream_t stream_) {
+static int full_op(const float *costs, int64_t B, int N, int M, int64_t *out,
+                   void *workspace, tm_stream_t stream_, int compact) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
     if (B == 0 || N == 0) return TM_OK;
     if (!out || !workspace) return TM_ERR_ARG;
     const int K = N > M ? N : M;
     if (K > tm_jv_max_k()) return TM_ERR_TOO_LARGE;
-    if (M == 0) return tm_jv_solve_f32(costs, B, N, M, 0.0f, 0, out, workspace, stream_);
+    if (M == 0) return solve_impl(costs, B, N, M, 0.0f, 0, 0, out, workspace, stream_);
     tmjv::StreamDevice scope(stream);
     if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
     // one pass solves every all-finite problem and gathers the statistics
-    int rc = tm_jv_solve_checked_f32(costs, B, N, M, out, workspace, stream_);
+    int rc = solve_impl(costs, B, N, M, 0.0f, 0, 1, out, workspace, stream_, nullptr, 0, compact);
     if (rc) return rc;
     tm_jv_stats h{};
     const tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
@@ -1473,8 +1496,20 @@ int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64
     rc = tm_jv_sentinel(&h, K, &sentinel, &pinf);
     if (rc) return rc;
     // +inf cells need the batch-global sentinel: solve again with it
-    if (pinf) return tm_jv_solve_f32(costs, B, N, M, sentinel, 1, out, workspace, stream_);
+    if (pinf)
+        return solve_impl(costs, B, N, M, sentinel, 1, 0, out, workspace, stream_, nullptr, 0,
+                          compact);
     return TM_OK;
+}
+
+int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64_t *out,
+                              void *workspace, tm_stream_t stream_) {
+    return full_op(costs, B, N, M, out, workspace, stream_, 0);
+}
+
+int tm_jonker_compact_batch_f32(const float *costs, int64_t B, int N, int M, int64_t *out,
+                                void *workspace, tm_stream_t stream_) {
+    return full_op(costs, B, N, M, out, workspace, stream_, 1);
 }
 
 int tm_jonker_dense_batch_async_f32(const float *costs, int64_t B, int N, int M,
@@ -1489,9 +1524,9 @@ int tm_jonker_dense_batch_async_f32(const float *costs, int64_t B, int N, int M,
     return solve_impl(costs, B, N, M, 0.0f, 0, 0, out, workspace, stream_, nullptr, 1);
 }
 
-int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int M,
-                                       const tm_jv_unpacked *u, void *workspace,
-                                       tm_stream_t stream_) {
+static int full_unpacked(const float *costs, int64_t B, int N, int M,
+                         const tm_jv_unpacked *u, void *workspace, tm_stream_t stream_,
+                         int compact) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (B < 0 || N <= 0 || M <= 0) return B == 0 ? TM_OK : TM_ERR_ARG;
     if (B == 0) return TM_OK;
@@ -1500,7 +1535,7 @@ int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int
     if (K > tm_jv_max_k()) return TM_ERR_TOO_LARGE;
     tmjv::StreamDevice scope(stream);
     if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
-    int rc = solve_impl(costs, B, N, M, 0.0f, 0, 1, nullptr, workspace, stream_, u);
+    int rc = solve_impl(costs, B, N, M, 0.0f, 0, 1, nullptr, workspace, stream_, u, 0, compact);
     if (rc) return rc;
     tm_jv_stats h{};
     const tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
@@ -1512,8 +1547,22 @@ int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int
     int pinf = 0;
     rc = tm_jv_sentinel(&h, K, &sentinel, &pinf);
     if (rc) return rc;
-    if (pinf) return solve_impl(costs, B, N, M, sentinel, 1, 0, nullptr, workspace, stream_, u);
+    if (pinf)
+        return solve_impl(costs, B, N, M, sentinel, 1, 0, nullptr, workspace, stream_, u, 0,
+                          compact);
     return TM_OK;
+}
+
+int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int M,
+                                       const tm_jv_unpacked *u, void *workspace,
+                                       tm_stream_t stream_) {
+    return full_unpacked(costs, B, N, M, u, workspace, stream_, 0);
+}
+
+int tm_jonker_compact_batch_unpacked_f32(const float *costs, int64_t B, int N, int M,
+                                         const tm_jv_unpacked *u, void *workspace,
+                                         tm_stream_t stream_) {
+    return full_unpacked(costs, B, N, M, u, workspace, stream_, 1);
 }
 
 }  // extern "C"

@@ -47,60 +47,47 @@ std::string status_text(int rc) {
     return s;
 }
 
-at::Tensor jonker_dense_batch_cuda(const at::Tensor &costs) {
+using FullFn = int (*)(const float *, int64_t, int, int, int64_t *, void *, tm_stream_t);
+using UnpackedFn = int (*)(const float *, int64_t, int, int, const tm_jv_unpacked *, void *,
+                           tm_stream_t);
+
+// Shared body of the packed ops: checks, capture guard, fp32 cast, then one
+// C-ABI call that solves in check mode, reads the 8-byte verdict back
+// (raising on NaN / -inf like cuda_common.cuh:245-249) and, only for a
+// batch holding +inf, solves again with the batch-global sentinel.
+at::Tensor packed_op(const at::Tensor &costs, FullFn fn, const char *name) {
     TORCH_CHECK(costs.is_cuda(), "costs must be a CUDA tensor");
     TORCH_CHECK(costs.dim() == 3, "costs must be 3D (B, N, M), got ", costs.dim());
     TORCH_CHECK(costs.scalar_type() == at::kFloat || costs.scalar_type() == at::kDouble,
                 "costs must be float32 or float64, got ", costs.scalar_type());
     const c10::cuda::CUDAGuard guard(costs.device());
-
-    const int64_t B = costs.size(0);
-    const int64_t N = costs.size(1);
-    const int64_t M = costs.size(2);
+    const int64_t B = costs.size(0), N = costs.size(1), M = costs.size(2);
     if (B == 0 || N == 0 || M == 0)
         return at::full({B, N}, -1, costs.options().dtype(at::kLong));
     const int64_t K = std::max(N, M);
     TORCH_CHECK(K <= tm_jv_max_k(), "Batched JV (CUDA) supports max(N, M) <= ", tm_jv_max_k(),
                 ", got K=", K);
-
     cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
-    check_not_capturing(stream, "jonker_dense_batch");
-
+    check_not_capturing(stream, name);
     const at::Tensor c = costs.to(at::kFloat).contiguous();
-    const float *cp = c.const_data_ptr<float>();
-    auto stream_h = reinterpret_cast<tm_stream_t>(stream);
-
-    // one small scratch block: batch statistics + the solve's work ticket
     at::Tensor scratch =
         at::empty({(int64_t)tm_jv_workspace_bytes()}, c.options().dtype(at::kByte));
-    auto *ws = reinterpret_cast<tm_jv_workspace *>(scratch.mutable_data_ptr());
-    auto *st_dev = &ws->stats;
-    // one pass solves every all-finite problem and gathers the statistics;
-    // the host then raises on NaN / -inf (reference cuda_common.cuh:245-249)
-    // or, if the batch holds +inf, solves again with the global sentinel
     at::Tensor out = at::empty({B, N}, costs.options().dtype(at::kLong));
-    int64_t *op = out.mutable_data_ptr<int64_t>();
-    int rc = tm_jv_solve_checked_f32(cp, B, static_cast<int>(N), static_cast<int>(M), op, ws,
-                                     stream_h);
+    const int rc = fn(c.const_data_ptr<float>(), B, static_cast<int>(N), static_cast<int>(M),
+                      out.mutable_data_ptr<int64_t>(), scratch.mutable_data_ptr(),
+                      reinterpret_cast<tm_stream_t>(stream));
+    TORCH_CHECK(rc != TM_ERR_NAN, name, ": ", tm_status_string(rc));
+    TORCH_CHECK(rc != TM_ERR_NEG_INF, name, ": ", tm_status_string(rc));
     TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
-    tm_jv_stats host{};
-    cudaError_t e =
-        cudaMemcpyAsync(&host, st_dev, sizeof(host), cudaMemcpyDeviceToHost, stream);
-    TORCH_CHECK(e == cudaSuccess, "batched JV statistics copy failed: ", cudaGetErrorString(e));
-    e = cudaStreamSynchronize(stream);
-    TORCH_CHECK(e == cudaSuccess, "batched JV statistics sync failed: ", cudaGetErrorString(e));
-    float sentinel = 1.0f;
-    int has_pos_inf = 0;
-    rc = tm_jv_sentinel(&host, static_cast<int>(K), &sentinel, &has_pos_inf);
-    TORCH_CHECK(rc != TM_ERR_NAN, "jonker_dense_batch: ", tm_status_string(rc));
-    TORCH_CHECK(rc != TM_ERR_NEG_INF, "jonker_dense_batch: ", tm_status_string(rc));
-    TORCH_CHECK(rc == TM_OK, "jonker_dense_batch: ", status_text(rc));
-    if (has_pos_inf) {
-        rc = tm_jv_solve_f32(cp, B, static_cast<int>(N), static_cast<int>(M), sentinel, 1, op,
-                             ws, stream_h);
-        TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
-    }
     return out;
+}
+
+at::Tensor jonker_dense_batch_cuda(const at::Tensor &costs) {
+    return packed_op(costs, &tm_jonker_dense_batch_f32, "jonker_dense_batch");
+}
+
+at::Tensor jonker_compact_batch_cuda(const at::Tensor &costs) {
+    return packed_op(costs, &tm_jonker_compact_batch_f32, "jonker_compact_batch");
 }
 
 // jonker_dense_batch_unpacked on CUDA (the reference has it on CPU only,
@@ -108,7 +95,7 @@ at::Tensor jonker_dense_batch_cuda(const at::Tensor &costs) {
 // the solve kernel's output stage.  Layout and empty-shape behaviour follow
 // the CPU op (cpu/ops.cpp:290-316).
 std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor>
-jonker_dense_batch_unpacked_cuda(const at::Tensor &costs) {
+unpacked_op(const at::Tensor &costs, UnpackedFn fn, const char *name) {
     TORCH_CHECK(costs.is_cuda(), "costs must be a CUDA tensor");
     TORCH_CHECK(costs.dim() == 3, "costs must be 3D (B, N, M), got ", costs.dim());
     TORCH_CHECK(costs.scalar_type() == at::kFloat || costs.scalar_type() == at::kDouble,
@@ -123,7 +110,7 @@ jonker_dense_batch_unpacked_cuda(const at::Tensor &costs) {
     TORCH_CHECK(K <= tm_jv_max_k(), "Batched JV (CUDA) supports max(N, M) <= ", tm_jv_max_k(),
                 ", got K=", K);
     cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
-    check_not_capturing(stream, "jonker_dense_batch_unpacked");
+    check_not_capturing(stream, name);
     const at::Tensor c = costs.to(at::kFloat).contiguous();
     at::Tensor scratch =
         at::empty({(int64_t)tm_jv_workspace_bytes()}, c.options().dtype(at::kByte));
@@ -131,13 +118,24 @@ jonker_dense_batch_unpacked_cuda(const at::Tensor &costs) {
     at::Tensor uc = at::empty({B, M}, lo), nm = at::empty({B}, lo);
     tm_jv_unpacked u{matches.mutable_data_ptr<int64_t>(), ur.mutable_data_ptr<int64_t>(),
                      uc.mutable_data_ptr<int64_t>(), nm.mutable_data_ptr<int64_t>()};
-    const int rc = tm_jonker_dense_batch_unpacked_f32(
+    const int rc = fn(
         c.const_data_ptr<float>(), B, static_cast<int>(N), static_cast<int>(M), &u,
         scratch.mutable_data_ptr(), reinterpret_cast<tm_stream_t>(stream));
-    TORCH_CHECK(rc != TM_ERR_NAN, "jonker_dense_batch_unpacked: ", tm_status_string(rc));
-    TORCH_CHECK(rc != TM_ERR_NEG_INF, "jonker_dense_batch_unpacked: ", tm_status_string(rc));
+    TORCH_CHECK(rc != TM_ERR_NAN, name, ": ", tm_status_string(rc));
+    TORCH_CHECK(rc != TM_ERR_NEG_INF, name, ": ", tm_status_string(rc));
     TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
     return {matches, ur, uc, nm};
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor>
+jonker_dense_batch_unpacked_cuda(const at::Tensor &costs) {
+    return unpacked_op(costs, &tm_jonker_dense_batch_unpacked_f32, "jonker_dense_batch_unpacked");
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor, at::Tensor>
+jonker_compact_batch_unpacked_cuda(const at::Tensor &costs) {
+    return unpacked_op(costs, &tm_jonker_compact_batch_unpacked_f32,
+                       "jonker_compact_batch_unpacked");
 }
 
 // jonker_dense_batch_async: the same mapping without any host
@@ -181,4 +179,6 @@ TORCH_LIBRARY_IMPL(assignment, CUDA, m) {
     m.impl("jonker_dense_batch_async", &jonker_dense_batch_async_cuda);
     m.impl("jonker_dense_batch", &jonker_dense_batch_cuda);
     m.impl("jonker_dense_batch_unpacked", &jonker_dense_batch_unpacked_cuda);
+    m.impl("jonker_compact_batch", &jonker_compact_batch_cuda);
+    m.impl("jonker_compact_batch_unpacked", &jonker_compact_batch_unpacked_cuda);
 }
