@@ -181,6 +181,13 @@ int tm_jonker_compact_batch_unpacked_f32(const float *costs, int64_t B, int N, i
                                          const tm_jv_unpacked *u, void *workspace,
                                          tm_stream_t stream);
 
+/* Test hook: caps every loop of the solver at `bound` iterations (0 restores
+ * the real bounds), so tests can drive the loop-bound failure path -- rows
+ * of -1 and TM_WS_UNSOLVED in the workspace status -- without a GPU fault.
+ * Process-wide; not for production use.  No counterpart in the reference
+ * (its CPU solver maps rc != 0 to a row of -1, cpu/ops.cpp:274-278). */
+void tm_jv_debug_set_loop_bound(int bound);
+
 /* The cudaError_t of the last TM_ERR_CUDA on this thread. */
 int tm_last_cuda_error(void);
 

@@ -25,7 +25,7 @@ def _core():
 def test_library_exports_every_declared_symbol():
     from torchmatch_b200 import _loader
 
-    declared = set(re.findall(r"^\s*(?:int|size_t|const char \*)\s*(tm_\w+)\(",
+    declared = set(re.findall(r"^\s*(?:int|void|size_t|const char \*)\s*(tm_\w+)\(",
                               HEADER.read_text(), re.M))
     assert declared == set(_loader.EXPORTED)
     lib = ctypes.CDLL(str(_loader.CORE_LIB))

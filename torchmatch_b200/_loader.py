@@ -115,6 +115,8 @@ def core() -> ctypes.CDLL:
     lib.tm_jonker_compact_batch_f32.restype = i32
     lib.tm_jonker_compact_batch_unpacked_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
     lib.tm_jonker_compact_batch_unpacked_f32.restype = i32
+    lib.tm_jv_debug_set_loop_bound.argtypes = [i32]
+    lib.tm_jv_debug_set_loop_bound.restype = None
     lib.tm_status_string.restype = ctypes.c_char_p
     lib.tm_status_string.argtypes = [i32]
     for name in ("tm_jv_stats_f32", "tm_jv_sentinel", "tm_jv_solve_f32",
@@ -138,5 +140,6 @@ EXPORTED = (
     "tm_jonker_compact_batch_f32",
     "tm_jonker_compact_batch_unpacked_f32",
     "tm_last_cuda_error",
+    "tm_jv_debug_set_loop_bound",
     "tm_status_string",
 )

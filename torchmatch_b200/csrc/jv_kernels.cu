@@ -77,6 +77,7 @@ struct Params {
     int check;                   // check mode: classify cells, bail on non-finite
     int compact;                 // jonker_compact_batch semantics (compact_core.h)
     int l2_prefetch;             // streaming mode: prefetch each claimed problem into L2
+    int loop_bound;              // test hook: lower bound on the loop caps (0 = none)
     int gated;                   // run only if *stats shows +inf and no NaN / -inf;
                                  // the sentinel is then computed on the device
     int warp_bytes;      // shared-memory bytes per warp
@@ -393,10 +394,10 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     // ---- column reduction (jonker_dense_flat.h:129-144) -------------------
     int ymin[S];
     uint32_t chk_fl = 0, chk_mk = 0;  // check mode: cell classes, max finite key
-#pragma unroll
     // compact variant (jonker_compact_core.h:78-86) seeds each column with
     // row 0; a +inf seed with the same strict < gives exactly that
     const float seed = P.compact ? __int_as_float(0x7f800000) : kBig;
+#pragma unroll
     for (int s = 0; s < S; ++s) { v[s] = seed; ymin[s] = 0; }
     {
         const int nreal = N < K ? N : K;
@@ -566,8 +567,9 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         int kept = 0;
         // the dense rule `rr_cnt < current * n` bounds the visits by K*K + K;
         // the compact variant has no such rule, so its bound is a safety net
-        const unsigned cap = P.compact ? 64u * (unsigned)K * (unsigned)K + 4096u
-                                       : (unsigned)K * (unsigned)K + 2u * K + 8u;
+        unsigned cap = P.compact ? 64u * (unsigned)K * (unsigned)K + 4096u
+                                 : (unsigned)K * (unsigned)K + 2u * K + 8u;
+        if (P.loop_bound && (unsigned)P.loop_bound < cap) cap = (unsigned)P.loop_bound;
         int row = w.queue[0];
         while (head < (unsigned)nfree && visits < cap) {
             ++visits;
@@ -801,7 +803,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         __syncwarp();
         int lo = 0, hi = 0, sink = -1, iter = 0;
         float mind = 0.0f;
-        const int icap = 4 * K + 8;
+        const int icap = (P.loop_bound && P.loop_bound < 4 * K + 8) ? P.loop_bound : 4 * K + 8;
         while (sink < 0) {
             if (++iter > icap) { failed = true; break; }
             if (lo == hi) {
@@ -1103,7 +1105,6 @@ __global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ?
         P.sanitize = 1;
     }
     const int warp = threadIdx.x >> 5;
-    const int wpb = blockDim.x >> 5;
     WarpShared w = carve(smem_raw + (size_t)warp * P.warp_bytes, TILE ? P.tile_floats : 0, 32 * S,
                          !TILE);
     const int64_t per = (int64_t)P.N * P.M;
@@ -1187,6 +1188,8 @@ __global__ void __launch_bounds__(256) jv_stats_kernel(const float *__restrict__
 
 // ------------------------------------------------------------ host launch
 static thread_local int g_last_cuda = 0;
+// test hook (tm_jv_debug_set_loop_bound): caps every solver loop
+static int g_loop_bound = 0;
 
 static int cuda_fail(cudaError_t e) {
     g_last_cuda = (int)e;
@@ -1351,6 +1354,8 @@ extern "C" {
 
 int tm_jv_max_k(void) { return 32 * tmjv::kMaxSlots; }
 
+void tm_jv_debug_set_loop_bound(int bound) { tmjv::g_loop_bound = bound > 0 ? bound : 0; }
+
 int tm_last_cuda_error(void) { return tmjv::g_last_cuda; }
 
 const char *tm_status_string(int status) {
@@ -1446,6 +1451,7 @@ static int solve_impl(const float *costs, int64_t B, int N, int M, float sentine
     P.compact = compact;
     P.gated = gated;
     P.l2_prefetch = tmjv::l2_prefetch_enabled();
+    P.loop_bound = tmjv::g_loop_bound;
     P.stats = &ws->stats;
     P.out = out;
     if (u) {
