@@ -4,7 +4,7 @@
  *
  * These entry points replace the CUDA side of the reference's
  * torch.ops.assignment.jonker_dense_batch (tue-p8n/torchmatch 1.0.3,
- * sources/torchmatch/assignment/):
+ * sources/torchmatch/assignment/) and widen it:
  *
  *   tm_jv_stats_f32         replaces k_scan_sentinel_stats + the scan half of
  *                           compute_inf_sentinel  (cuda/cuda_common.cuh:186-243)
@@ -17,15 +17,26 @@
  *                           cuda/dispatch.cu:156-176); the result follows the
  *                           CPU solver (cpu/ops.cpp:176-289 +
  *                           cpu/jonker_dense_flat.h:124-274) bit for bit
+ *   tm_jv_solve_checked_f32 the solve with the statistics pass fused in
  *   tm_jonker_dense_batch_f32  the whole op body of jonker_dense_batch_cuda
  *                           (cuda/dispatch.cu:137-177) for callers without
- *                           torch: stats, host check, solve
+ *                           torch: one check-mode solve, host check, and a
+ *                           sentinel solve only for batches holding +inf
+ *   tm_jonker_dense_batch_unpacked_f32, tm_jonker_compact_batch_f32,
+ *   tm_jonker_compact_batch_unpacked_f32  the reference's CPU-only unpacked
+ *                           and compact ops (cpu/ops.cpp:297-417,
+ *                           cpu/jonker_compact_core.h) on the GPU
+ *   tm_jonker_dense_batch_async_f32  no host synchronisation (capturable)
+ *   tm_jonker_dense_batch_f32_noalloc  no allocation by the caller
  *
  * Conventions: plain device pointers and sizes, no torch types, no C++
  * exceptions.  Every function returns a tm_status code; CUDA errors are
  * reported as TM_ERR_CUDA and the cudaError_t is kept for tm_last_cuda_error().
- * All work is enqueued on the given stream; only tm_jonker_dense_batch_f32
- * synchronises it (to read the NaN / -inf verdict, as the reference does).
+ * Problems that hit a loop bound are reported through TM_WS_UNSOLVED in the
+ * workspace status (their rows are -1), not through the return code.  All
+ * work is enqueued on the given stream; only the whole-op entry points
+ * (tm_jonker_*_f32 except the async one) synchronise it, to read the
+ * NaN / -inf verdict as the reference does.
  */
 #ifndef TORCHMATCH_B200_H
 #define TORCHMATCH_B200_H
@@ -46,7 +57,7 @@ typedef enum tm_status {
     TM_ERR_ARG = 3,        /* bad shape / null pointer / unsupported size     */
     TM_ERR_CUDA = 4,       /* a CUDA call failed; see tm_last_cuda_error()    */
     TM_ERR_TOO_LARGE = 5,  /* max(N, M) above tm_jv_max_k()                    */
-    TM_ERR_UNSOLVED = 6    /* a problem hit a loop bound; its row is all -1    */
+    TM_ERR_UNSOLVED = 6    /* a problem hit a loop bound (see TM_WS_UNSOLVED)  */
 } tm_status;
 
 /* Batch statistics, device-resident.  Written by tm_jv_stats_f32. */
