@@ -28,6 +28,9 @@
  *                           cpu/jonker_compact_core.h) on the GPU
  *   tm_jonker_dense_batch_async_f32  no host synchronisation (capturable)
  *   tm_jonker_dense_batch_f32_noalloc  no allocation by the caller
+ *   tm_jonker_sqeuclidean_batch_f32  squared-Euclidean costs built from two
+ *                           point sets inside the solve kernel (no (B, N, M)
+ *                           cost tensor in memory)
  *
  * Conventions: plain device pointers and sizes, no torch types, no C++
  * exceptions.  Every function returns a tm_status code; CUDA errors are
@@ -191,6 +194,28 @@ int tm_jonker_compact_batch_f32(const float *costs, int64_t B, int N, int M, int
 int tm_jonker_compact_batch_unpacked_f32(const float *costs, int64_t B, int N, int M,
                                          const tm_jv_unpacked *u, void *workspace,
                                          tm_stream_t stream);
+
+/* Fused cost construction: solves jonker_dense_batch on the squared-
+ * Euclidean costs of two point sets, x (B, N, D) and y (B, M, D), both
+ * contiguous fp32 on the device, without writing the (B, N, M) cost batch.
+ * Cell (i, j) of problem b is the fp32 sum over d = 0 .. D-1, in that order,
+ * of (x[b][i][d] - y[b][j][d])^2, each subtraction, product and sum rounded
+ * separately (no fused multiply-add), starting from 0: the result equals
+ * tm_jonker_dense_batch_f32 on the matrix that such a sequential producer
+ * writes (the order of the reference's lazy sqeuclidean costs,
+ * transport/matrix/cpu/exact/network_simplex_simple.h:453-457, in fp32).
+ * NaN / -inf / +inf cells (from non-finite coordinates) behave as in the
+ * dense op.  `workspace` is 256-byte aligned device memory of
+ * `workspace_bytes` >= tm_jv_points_workspace_bytes(B, N, M) bytes
+ * (query on the device that will run the call): shapes whose problems fit
+ * in shared memory need only the 256-byte header; larger ones also take
+ * one N * M slab per resident warp (a smaller workspace runs fewer warps;
+ * TM_ERR_ARG below one slab).  No counterpart op in the reference, whose
+ * callers build the cost tensor first (tests/_costgen.py) and pass it. */
+size_t tm_jv_points_workspace_bytes(int64_t B, int N, int M);
+int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, int N, int M,
+                                    int D, int64_t *out, void *workspace,
+                                    size_t workspace_bytes, tm_stream_t stream);
 
 /* Test hook: caps every loop of the solver at `bound` iterations (0 restores
  * the real bounds), so tests can drive the loop-bound failure path -- rows

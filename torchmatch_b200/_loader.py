@@ -115,6 +115,11 @@ def core() -> ctypes.CDLL:
     lib.tm_jonker_compact_batch_f32.restype = i32
     lib.tm_jonker_compact_batch_unpacked_f32.argtypes = [vp, i64, i32, i32, vp, vp, vp]
     lib.tm_jonker_compact_batch_unpacked_f32.restype = i32
+    lib.tm_jv_points_workspace_bytes.argtypes = [i64, i32, i32]
+    lib.tm_jv_points_workspace_bytes.restype = ctypes.c_size_t
+    lib.tm_jonker_sqeuclidean_batch_f32.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp,
+                                                   ctypes.c_size_t, vp]
+    lib.tm_jonker_sqeuclidean_batch_f32.restype = i32
     lib.tm_jv_debug_set_loop_bound.argtypes = [i32]
     lib.tm_jv_debug_set_loop_bound.restype = None
     lib.tm_status_string.restype = ctypes.c_char_p
@@ -139,6 +144,8 @@ EXPORTED = (
     "tm_jonker_dense_batch_async_f32",
     "tm_jonker_compact_batch_f32",
     "tm_jonker_compact_batch_unpacked_f32",
+    "tm_jv_points_workspace_bytes",
+    "tm_jonker_sqeuclidean_batch_f32",
     "tm_last_cuda_error",
     "tm_jv_debug_set_loop_bound",
     "tm_status_string",

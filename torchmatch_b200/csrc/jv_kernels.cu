@@ -80,6 +80,15 @@ struct Params {
     int loop_bound;              // test hook: lower bound on the loop caps (0 = none)
     int gated;                   // run only if *stats shows +inf and no NaN / -inf;
                                  // the sentinel is then computed on the device
+    // fused squared-Euclidean costs: x (B, N, D) and y (B, M, D) replace
+    // `costs`; streaming shapes give each resident warp a slab of N * M
+    // floats at slab + (global warp index) * slab_floats
+    const float *px;
+    const float *py;
+    int D;
+    float *slab;
+    int64_t slab_floats;
+    int64_t slab_warps;  // slabs available in the workspace (host side)
     int warp_bytes;      // shared-memory bytes per warp
     int tile_floats;     // floats reserved for the staged tile (TILE mode)
     int bulk_ok;         // tile base and size are 16-byte multiples
@@ -226,7 +235,16 @@ __device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP,
 // stride M), zeros in the padding (cpu/ops.cpp:262-270).  In streaming mode
 // +inf cells become the sentinel here; in TILE mode the tile was already
 // sanitised.
-template <int S, int VEC, bool TILE, bool FULL>
+// Read-only loads of the input batch go through the non-coherent path.  Rows
+// of a points slab (PTS) were written earlier in the same launch, which that
+// path does not allow, so they are read with L2-only loads instead.
+template <bool PTS, class T>
+__device__ __forceinline__ T gload(const T *p) {
+    if constexpr (PTS) return __ldcg(p);
+    else return __ldg(p);
+}
+
+template <int S, int VEC, bool TILE, bool FULL, bool PTS = false>
 __device__ __forceinline__ void load_row(const float *__restrict__ src, int i, int N, int M,
                                          int lane, bool sanitize, float sentinel,
                                          float (&c)[S]) {
@@ -240,14 +258,14 @@ __device__ __forceinline__ void load_row(const float *__restrict__ src, int i, i
             const float *q = row + g * 32 * VEC;
             if constexpr (VEC == 4) {
                 const float4 t = TILE ? *reinterpret_cast<const float4 *>(q)
-                                      : __ldg(reinterpret_cast<const float4 *>(q));
+                                      : gload<PTS>(reinterpret_cast<const float4 *>(q));
                 c[g * 4 + 0] = t.x; c[g * 4 + 1] = t.y; c[g * 4 + 2] = t.z; c[g * 4 + 3] = t.w;
             } else if constexpr (VEC == 2) {
                 const float2 t = TILE ? *reinterpret_cast<const float2 *>(q)
-                                      : __ldg(reinterpret_cast<const float2 *>(q));
+                                      : gload<PTS>(reinterpret_cast<const float2 *>(q));
                 c[g * 2 + 0] = t.x; c[g * 2 + 1] = t.y;
             } else {
-                c[g] = TILE ? *q : __ldg(q);
+                c[g] = TILE ? *q : gload<PTS>(q);
             }
         }
         if constexpr (!TILE) {
@@ -272,16 +290,16 @@ __device__ __forceinline__ void load_row(const float *__restrict__ src, int i, i
             if constexpr (VEC == 4) {
                 float4 t;
                 if constexpr (TILE) t = *reinterpret_cast<const float4 *>(row + j0);
-                else t = __ldg(reinterpret_cast<const float4 *>(row + j0));
+                else t = gload<PTS>(reinterpret_cast<const float4 *>(row + j0));
                 c[g * 4 + 0] = t.x; c[g * 4 + 1] = t.y; c[g * 4 + 2] = t.z; c[g * 4 + 3] = t.w;
             } else if constexpr (VEC == 2) {
                 float2 t;
                 if constexpr (TILE) t = *reinterpret_cast<const float2 *>(row + j0);
-                else t = __ldg(reinterpret_cast<const float2 *>(row + j0));
+                else t = gload<PTS>(reinterpret_cast<const float2 *>(row + j0));
                 c[g * 2 + 0] = t.x; c[g * 2 + 1] = t.y;
             } else {
                 if constexpr (TILE) c[g] = row[j0];
-                else c[g] = __ldg(row + j0);
+                else c[g] = gload<PTS>(row + j0);
             }
         } else {
 #pragma unroll
@@ -290,7 +308,7 @@ __device__ __forceinline__ void load_row(const float *__restrict__ src, int i, i
                 float val = 0.0f;
                 if (j < M) {
                     if constexpr (TILE) val = row[j];
-                    else val = __ldg(row + j);
+                    else val = gload<PTS>(row + j);
                 }
                 c[g * VEC + e] = val;
             }
@@ -301,6 +319,61 @@ __device__ __forceinline__ void load_row(const float *__restrict__ src, int i, i
 #pragma unroll
             for (int s = 0; s < S; ++s)
                 if (isinf(c[s])) c[s] = sentinel;
+        }
+    }
+}
+
+// Fused cost construction: cell (i, j) of one problem is
+//   sum over d = 0 .. D-1, in that order, of (x[i][d] - y[j][d])^2
+// in fp32, every subtraction, product and sum rounded on its own (no fused
+// multiply-add), starting from 0.  That is the squared-Euclidean producer of
+// the reference's lazy costs (transport/matrix/cpu/exact/
+// network_simplex_simple.h:453-457) in single precision, so the solve sees
+// exactly the matrix that a sequential fp32 producer would have written.
+// Each lane owns columns lane + 32 t; their points are held in registers 8
+// coordinates at a time while the rows stream past (x row: one broadcast
+// load per coordinate).  Partial sums of later coordinate chunks are added to
+// the stored value, which keeps the summation order.  +inf cells become the
+// sentinel when the batch needs it (sanitize).  `dst` has row stride M.
+__device__ void fill_points(float *dst, const float *__restrict__ x,
+                            const float *__restrict__ y, int N, int M, int D, int lane,
+                            bool sanitize, float sentinel) {
+    constexpr int kCols = 4, kDims = 8;
+    const int dend = D > 0 ? D : 1;  // D == 0: one pass that stores zeros
+    for (int j0 = 0; j0 < M; j0 += 32 * kCols) {
+        for (int d0 = 0; d0 < dend; d0 += kDims) {
+            const int dn = D - d0 < kDims ? D - d0 : kDims;
+            const bool last = d0 + kDims >= dend;
+            float yv[kCols][kDims];
+#pragma unroll
+            for (int t = 0; t < kCols; ++t) {
+                const int j = j0 + t * 32 + lane;
+#pragma unroll
+                for (int e = 0; e < kDims; ++e)
+                    yv[t][e] = (j < M && e < dn) ? __ldg(y + (int64_t)j * D + d0 + e) : 0.0f;
+            }
+            for (int i = 0; i < N; ++i) {
+                float xv[kDims];
+#pragma unroll
+                for (int e = 0; e < kDims; ++e)
+                    xv[e] = e < dn ? __ldg(x + (int64_t)i * D + d0 + e) : 0.0f;
+                float *row = dst + (int64_t)i * M;
+#pragma unroll
+                for (int t = 0; t < kCols; ++t) {
+                    const int j = j0 + t * 32 + lane;
+                    if (j < M) {
+                        float acc = d0 == 0 ? 0.0f : row[j];
+#pragma unroll
+                        for (int e = 0; e < kDims; ++e)
+                            if (e < dn) {
+                                const float df = __fsub_rn(xv[e], yv[t][e]);
+                                acc = __fadd_rn(acc, __fmul_rn(df, df));
+                            }
+                        if (last && sanitize && isinf(acc)) acc = sentinel;
+                        row[j] = acc;
+                    }
+                }
+            }
         }
     }
 }
@@ -365,7 +438,7 @@ __device__ void emit_result(const Params &P, WarpShared &w, int lane, int64_t b,
 }
 
 // ------------------------------------------------------------- one solve
-template <int S, int VEC, bool TILE, bool FULL>
+template <int S, int VEC, bool TILE, bool FULL, bool PTS>
 __device__ void solve_problem(const float *__restrict__ src, const Params &P, WarpShared &w,
                               int lane, int64_t b) {
     using L = Layout<S, VEC>;
@@ -405,8 +478,8 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
         const bool check = P.check != 0;
         for (; i + 2 <= nreal; i += 2) {
             float c0[S], c1[S];
-            load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c0);
-            load_row<S, VEC, TILE, FULL>(src, i + 1, N, M, lane, sanitize, sentinel, c1);
+            load_row<S, VEC, TILE, FULL, PTS>(src, i, N, M, lane, sanitize, sentinel, c0);
+            load_row<S, VEC, TILE, FULL, PTS>(src, i + 1, N, M, lane, sanitize, sentinel, c1);
 #pragma unroll
             for (int s = 0; s < S; ++s) {
                 if (c0[s] < v[s]) { v[s] = c0[s]; ymin[s] = i; }
@@ -422,7 +495,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             }
         }
         for (; i < nreal; ++i) {
-            load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c);
+            load_row<S, VEC, TILE, FULL, PTS>(src, i, N, M, lane, sanitize, sentinel, c);
 #pragma unroll
             for (int s = 0; s < S; ++s)
                 if (c[s] < v[s]) { v[s] = c[s]; ymin[s] = i; }
@@ -510,7 +583,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             const int i = s * 32 + __ffs(m) - 1;
             m &= m - 1;
             const int own = w.xrow[i];
-            load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c);
+            load_row<S, VEC, TILE, FULL, PTS>(src, i, N, M, lane, sanitize, sentinel, c);
             float loc = P.compact ? FLT_MAX : kBig;  // compact_core.h:104
 #pragma unroll
             for (int t = 0; t < S; ++t)
@@ -600,7 +673,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 hit = v2 < w.cbound[row] && v2 < big2;
             }
             if (!hit) {
-                load_row<S, VEC, TILE, FULL>(src, row, N, M, lane, sanitize, sentinel, c);
+                load_row<S, VEC, TILE, FULL, PTS>(src, row, N, M, lane, sanitize, sentinel, c);
                 if constexpr (use_cache) {
 #pragma unroll
                     for (int t = 0; t < S; ++t)
@@ -677,13 +750,8 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 vj1 = w.vsh[j1];
                 i0 = w.ycol[j1];
             } else {
-                if constexpr (use_cache) {
-                    vj1 = w.vsh[j1];
-                    i0 = w.ycol[j1];
-                } else {
-                    vj1 = __shfl_sync(kFull, sel(v, s1), l1);
-                    i0 = __shfl_sync(kFull, seli(yc, s1), l1);
-                }
+                vj1 = __shfl_sync(kFull, sel(v, s1), l1);
+                i0 = __shfl_sync(kFull, seli(yc, s1), l1);
             }
             if (__builtin_expect(!(v2 < big2), 0)) {
                 // a reduced cost at or above LARGE: replay the scalar scan
@@ -788,7 +856,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     // ---- shortest augmenting paths (:75-122, :237-258) -------------------
     for (int f = 0; f < nfree && !failed; ++f) {
         const int start = w.queue[f];
-        load_row<S, VEC, TILE, FULL>(src, start, N, M, lane, sanitize, sentinel, c);
+        load_row<S, VEC, TILE, FULL, PTS>(src, start, N, M, lane, sanitize, sentinel, c);
         unsigned todo = valid, ready = 0, grp = 0;
 #pragma unroll
         for (int s = 0; s < S; ++s) {
@@ -936,7 +1004,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 const float dj = w.dist[j];
                 const int lj = L::lane_of(j), sj = L::slot_of(j);
                 const float vj = __shfl_sync(kFull, sel(v, sj), lj);
-                load_row<S, VEC, TILE, FULL>(src, i, N, M, lane, sanitize, sentinel, c);
+                load_row<S, VEC, TILE, FULL, PTS>(src, i, N, M, lane, sanitize, sentinel, c);
                 const float cij = __shfl_sync(kFull, sel(c, sj), lj);
                 const float h = cij - vj - dj;
                 unsigned ev = 0;
@@ -1081,7 +1149,7 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
 }
 
 // ------------------------------------------------------------------ kernel
-template <int S, int VEC, bool TILE, bool FULL>
+template <int S, int VEC, bool TILE, bool FULL, bool PTS>
 __global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ? 1 : 4) jv_batch_kernel(const Params P0) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
@@ -1129,7 +1197,21 @@ __global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ?
         const float *g = P.costs + b * per;
         const float *src = g;
         TMJV_T(t_load);
-        if constexpr (TILE) {
+        if constexpr (PTS) {
+            // streaming shape, fused costs: build the problem in this warp's slab
+            static_assert(!TILE, "points in TILE mode use the shared-memory tile");
+            float *slab = P.slab + ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * P.slab_floats;
+            fill_points(slab, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D, P.N,
+                        P.M, P.D, lane, P.sanitize != 0, P.sentinel);
+            __syncwarp();  // orders the lanes' slab stores before the row reads
+            src = slab;
+        } else if (TILE && P.px) {
+            // TILE shape, fused costs: build the problem in the tile itself
+            fill_points(w.tile, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D,
+                        P.N, P.M, P.D, lane, P.sanitize != 0, P.sentinel);
+            __syncwarp();
+            src = w.tile;
+        } else if constexpr (TILE) {
             bool ok = true;
             if (P.bulk_ok) {
                 if (lane == 0) bulk_load(w.tile, g, tile_bytes, w.bar);
@@ -1155,7 +1237,7 @@ __global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ?
             if (P.l2_prefetch && P.bulk_ok && lane == 0) prefetch_l2(g, tile_bytes);
         }
         TMJV_ACC(0, t_load);
-        solve_problem<S, VEC, TILE, FULL>(src, P, w, lane, b);
+        solve_problem<S, VEC, TILE, FULL, PTS>(src, P, w, lane, b);
         b = nb;
     }
 }
@@ -1260,7 +1342,7 @@ static int tile_min_warps() {
 }
 constexpr int kMaxWarpsPerBlock = 16;
 
-template <int S, int VEC, bool TILE, bool FULL>
+template <int S, int VEC, bool TILE, bool FULL, bool PTS = false>
 static int launch_t(const Params &P0, cudaStream_t stream) {
     Params P = P0;
     const int KP = 32 * S;
@@ -1276,7 +1358,7 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     const int64_t need_warps = P.B;
     if ((int64_t)wpb > need_warps) wpb = (int)need_warps;
     const int smem = wpb * warp_bytes;
-    auto kern = jv_batch_kernel<S, VEC, TILE, FULL>;
+    auto kern = jv_batch_kernel<S, VEC, TILE, FULL, PTS>;
     // The shared-memory opt-in and the occupancy query run once per device
     // and launch shape, so a steady-state launch is just the kernel (nothing
     // that a CUDA graph capture would reject).
@@ -1306,6 +1388,11 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     int64_t blocks = (P.B + wpb - 1) / wpb;
     const int64_t resident = (int64_t)num_sms() * per_sm;
     if (blocks > resident) blocks = resident;
+    if (PTS) {
+        // one slab per resident warp: fewer slabs, fewer blocks
+        if (P.slab_warps < wpb) return TM_ERR_ARG;
+        if (blocks * wpb > P.slab_warps) blocks = P.slab_warps / wpb;
+    }
     kern<<<(unsigned)blocks, wpb * 32, smem, stream>>>(P);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
@@ -1332,6 +1419,21 @@ static int launch(Params P, cudaStream_t stream) {
 #define TM_F(SS, VV)                                                                     \
     return tile ? launch_t<SS, VV, true, true>(P, stream)                                \
                 : launch_t<SS, VV, false, true>(P, stream)
+    if (P.px && !tile) {
+        // fused costs, streaming shape: rows come from the warp slabs, which
+        // are 256-byte aligned with row stride M
+        const bool s4 = P.M % 4 == 0;
+#define TM_P(SS, VV, FF) return launch_t<SS, VV, false, FF, true>(P, stream)
+        switch (S) {
+        case 4: if (full && s4) { TM_P(4, 4, true); } if (s4) { TM_P(4, 4, false); } TM_P(4, 1, false);
+        case 5: TM_P(5, 1, false);
+        case 6: TM_P(6, 1, false);
+        case 7: TM_P(7, 1, false);
+        case 8: if (full && s4) { TM_P(8, 4, true); } if (s4) { TM_P(8, 4, false); } TM_P(8, 1, false);
+        default: return TM_ERR_ARG;  // smaller shapes always fit the tile
+        }
+#undef TM_P
+    }
     switch (S) {
     case 1: if (full) { TM_F(1, 1); } TM_L(1, 1);
     case 2: if (full && v2) { TM_F(2, 2); } if (v2) { TM_L(2, 2); } TM_L(2, 1);
@@ -1345,6 +1447,47 @@ static int launch(Params P, cudaStream_t stream) {
     }
 #undef TM_L
 #undef TM_F
+}
+
+// Fused squared-Euclidean inputs of one call (host side).
+struct Points {
+    const float *x;
+    const float *y;
+    int D;
+    float *slab;
+    int64_t slab_floats;
+    int64_t slab_warps;
+};
+
+constexpr size_t kPointsHeader = 256;  // tm_jv_workspace, padded to the slab alignment
+
+// Floats of one warp slab (a multiple of 64, so every slab is 256-byte aligned).
+static int64_t points_slab_floats(int N, int M) {
+    return ((int64_t)N * M + 63) / 64 * 64;
+}
+
+// Slabs a fused call of this shape uses on the current device: none for
+// shapes solved in the shared-memory tile, else one per resident warp (an
+// upper bound of the launch's residency: shared memory, the block size and
+// the blocks per SM of the launch bounds).
+static int64_t points_slabs(int64_t B, int N, int M) {
+    const int K = N > M ? N : M;
+    const int S = slots_for(K);
+    const int64_t per = (int64_t)N * M;
+    const int64_t tile_bytes = ((per + 31) / 32 * 32) * 4 + book_bytes(32 * S, false);
+    if (tile_bytes * tile_min_warps() <= kSmemLimit || B <= 0) return 0;
+    const int warp_bytes = (book_bytes(32 * S, true) + 127) & ~127;
+    int wpb = kSmemLimit / warp_bytes;
+    const int cap = S > 4 ? kMaxWarpsPerBlock : 8;
+    if (wpb > cap) wpb = cap;
+    if ((int64_t)wpb > B) wpb = (int)B;
+    int per_sm = S > 4 ? 1 : 4;
+    const int fit = (228 * 1024) / (wpb * warp_bytes);
+    if (fit < per_sm) per_sm = fit > 0 ? fit : 1;
+    int64_t blocks = (B + wpb - 1) / wpb;
+    const int64_t resident = (int64_t)num_sms() * per_sm;
+    if (blocks > resident) blocks = resident;
+    return blocks * wpb;
 }
 
 }  // namespace tmjv
@@ -1410,11 +1553,11 @@ int tm_jv_sentinel(const tm_jv_stats *st, int K, float *sentinel, int *has_pos_i
 static int solve_impl(const float *costs, int64_t B, int N, int M, float sentinel,
                       int has_pos_inf, int check, int64_t *out, void *workspace,
                       tm_stream_t stream_, const tm_jv_unpacked *u = nullptr,
-                      int gated = 0, int compact = 0) {
+                      int gated = 0, int compact = 0, const tmjv::Points *pts = nullptr) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
     if (B == 0 || N == 0) return TM_OK;
-    if ((!out && !u) || !workspace || (M > 0 && !costs)) return TM_ERR_ARG;
+    if ((!out && !u) || !workspace || (M > 0 && !costs && !pts)) return TM_ERR_ARG;
     if (u && (!u->matches || !u->unmatched_rows || !u->unmatched_cols || !u->n_matched))
         return TM_ERR_ARG;
     const int K = N > M ? N : M;
@@ -1462,6 +1605,14 @@ static int solve_impl(const float *costs, int64_t B, int N, int M, float sentine
     }
     P.status = &ws->status;
     P.ticket = &ws->ticket;
+    if (pts) {
+        P.px = pts->x;
+        P.py = pts->y;
+        P.D = pts->D;
+        P.slab = pts->slab;
+        P.slab_floats = pts->slab_floats;
+        P.slab_warps = pts->slab_warps;
+    }
     return tmjv::launch(P, stream);
 }
 
@@ -1569,6 +1720,56 @@ int tm_jonker_compact_batch_unpacked_f32(const float *costs, int64_t B, int N, i
                                          const tm_jv_unpacked *u, void *workspace,
                                          tm_stream_t stream_) {
     return full_unpacked(costs, B, N, M, u, workspace, stream_, 1);
+}
+
+size_t tm_jv_points_workspace_bytes(int64_t B, int N, int M) {
+    if (B <= 0 || N <= 0 || M <= 0 || (N > M ? N : M) > tm_jv_max_k())
+        return tmjv::kPointsHeader;
+    return tmjv::kPointsHeader +
+           (size_t)tmjv::points_slabs(B, N, M) * (size_t)tmjv::points_slab_floats(N, M) * 4;
+}
+
+int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, int N, int M,
+                                    int D, int64_t *out, void *workspace,
+                                    size_t workspace_bytes, tm_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (B < 0 || N < 0 || M < 0 || D < 0) return TM_ERR_ARG;
+    if (B == 0 || N == 0) return TM_OK;
+    if (!out || !workspace || workspace_bytes < tmjv::kPointsHeader) return TM_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return TM_ERR_ARG;
+    const int K = N > M ? N : M;
+    if (K > tm_jv_max_k()) return TM_ERR_TOO_LARGE;
+    if (M == 0) return solve_impl(nullptr, B, N, M, 0.0f, 0, 0, out, workspace, stream_);
+    if (D > 0 && (!x || !y)) return TM_ERR_ARG;
+    tmjv::StreamDevice scope(stream);
+    if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
+    tmjv::Points pts{x, y, D, nullptr, tmjv::points_slab_floats(N, M), 0};
+    if (tmjv::points_slabs(B, N, M) > 0) {
+        pts.slab = reinterpret_cast<float *>(static_cast<unsigned char *>(workspace) +
+                                             tmjv::kPointsHeader);
+        pts.slab_warps = (int64_t)((workspace_bytes - tmjv::kPointsHeader) / 4) / pts.slab_floats;
+        if (pts.slab_warps < 1) return TM_ERR_ARG;
+    }
+    // check mode: every all-finite problem is solved and the statistics of
+    // the computed cells are gathered in the same pass
+    int rc = solve_impl(nullptr, B, N, M, 0.0f, 0, 1, out, workspace, stream_, nullptr, 0, 0,
+                        &pts);
+    if (rc) return rc;
+    tm_jv_stats h{};
+    const tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
+    cudaError_t e = cudaMemcpyAsync(&h, st, sizeof(h), cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    float sentinel = 1.0f;
+    int pinf = 0;
+    rc = tm_jv_sentinel(&h, K, &sentinel, &pinf);
+    if (rc) return rc;
+    // +inf cells (coordinates at +-inf) need the batch-global sentinel
+    if (pinf)
+        return solve_impl(nullptr, B, N, M, sentinel, 1, 0, out, workspace, stream_, nullptr, 0, 0,
+                          &pts);
+    return TM_OK;
 }
 
 }  // extern "C"
