@@ -412,6 +412,105 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_fused(args):
+    """Fused cost construction (jonker_sqeuclidean_batch) on the config-5
+    problem set: x, y ~ N(0, I16) point sets of 256 points, B problems.
+    Reported beside the dense op on the same problems with the (B, 256, 256)
+    cost tensor already built (cost construction not timed there), so the
+    comparison is conservative.  One GPU."""
+    import torch
+
+    import torchmatch_b200  # noqa: F401
+    from torchmatch_b200 import _loader
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "ours", "unavailable": "--fused runs on one GPU"}))
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    b, n, d = args.batch or 65536, 256, 16
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(b, n, d, device=dev, generator=g)
+    y = torch.randn(b, n, d, device=dev, generator=g)
+    ops = torch.ops.assignment
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(steps):
+            fn()
+        t1.record()
+        torch.cuda.synchronize()
+        return t0.elapsed_time(t1) / steps
+
+    steps = max(3, min(args.steps, 10))
+    vis = (os.environ.get("CUDA_VISIBLE_DEVICES") or "0").split(",")[0]
+    clocks = ClockSampler(int(vis) if vis.isdigit() else 0)
+    clocks.start()
+    fused_ms = timed(lambda: ops.jonker_sqeuclidean_batch(x, y), steps)
+    clk = clocks.stop()
+    # kernel-only: the check-mode launch through the C ABI
+    lib = _loader.core()
+    nbytes = lib.tm_jv_points_workspace_bytes(b, n, n)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = torch.empty(b, n, dtype=torch.long, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def fused_abi():
+        rc = lib.tm_jonker_sqeuclidean_batch_f32(x.data_ptr(), y.data_ptr(), b, n, n, d,
+                                                 out.data_ptr(), ws.data_ptr(), nbytes, stream)
+        assert rc == 0, lib.tm_status_string(rc)
+    abi_ms = timed(fused_abi, steps)
+    # the same problems through the dense op, cost tensor pre-built
+    costs = torch.empty(b, n, n, device=dev)
+    for s0 in range(0, b, 1024):
+        s1 = min(b, s0 + 1024)
+        costs[s0:s1] = ((x[s0:s1, :, None] - y[s0:s1, None]) ** 2).sum(-1)
+    dense_ms = timed(lambda: ops.jonker_dense_batch(costs), steps)
+    del costs
+    # end to end: pinned host points in, mapping out, every step
+    hb = min(b, 16384)
+    hx, hy = x[:hb].cpu().pin_memory(), y[:hb].cpu().pin_memory()
+
+    def e2e_step():
+        ops.jonker_sqeuclidean_batch(hx.to(dev, non_blocking=True),
+                                     hy.to(dev, non_blocking=True)).cpu()
+    e2e_ms = timed(e2e_step, max(3, steps // 2))
+    peak, peak_src = peak_hbm()
+    alg = b * (2 * n * d * 4 + n * 8)
+    achieved = alg / (abi_ms / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": b / (fused_ms / 1e3), "unit": UNIT, "n_gpus": 1,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": fused_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": f"config5 problems from points: fused sqeuclidean costs, "
+                               f"B={b} N=M={n} D={d}, x,y~N(0,I16)",
+                   "global_batch": b, "parallelism": "single GPU",
+                   "l2": f"points {2 * b * n * d * 4 / 2**20:.0f} MiB, slabs "
+                         f"{nbytes / 2**20:.0f} MiB (> L2)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": None,
+                     "kernel": "jv_batch_kernel (points, check mode)",
+                     "avg_launch_us": abi_ms * 1e3, "alg_bytes_per_launch": alg,
+                     "peak_source": peak_src},
+        "dense_op_prebuilt_costs": {"value": b / (dense_ms / 1e3), "unit": UNIT,
+                                    "ms_per_step": dense_ms,
+                                    "cost_tensor_bytes": b * n * n * 4},
+        "e2e": {"value": hb / (e2e_ms / 1e3), "unit": UNIT,
+                "h2d_bytes_per_step": 2 * hb * n * d * 4, "d2h_bytes_per_step": hb * n * 8,
+                "problems_per_step": hb},
+        "gpu_launches": steps,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_once(args):
     """Two calls of the op on one resident batch, nothing timed: the case the
     committed ncu summaries under profiles/ were captured on."""
@@ -437,10 +536,14 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--once", action="store_true",
                     help="solve the workload twice and exit (a small case for ncu captures)")
-    ap.add_argument("--batch", type=int, default=0, help="override B (with --once)")
+    ap.add_argument("--batch", type=int, default=0, help="override B (with --once / --fused)")
+    ap.add_argument("--fused", action="store_true",
+                    help="fused squared-Euclidean cost construction on config-5 point sets")
     args = ap.parse_args()
     if args.once:
         run_once(args)
+    elif args.fused:
+        run_fused(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

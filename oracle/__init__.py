@@ -95,3 +95,30 @@ def reference_jonker_dense_batch(costs, threads: int = 0) -> np.ndarray:
 
 def host_threads() -> int:
     return len(os.sched_getaffinity(0))
+
+
+def sqeuclidean_costs(x, y) -> np.ndarray:
+    """Squared-Euclidean (B, N, M) fp32 costs of x (B, N, D) and y (B, M, D),
+    summed over d in order with every operation rounded (jv_oracle.c)."""
+    key = f"{LIB}:tmo_sqeuclidean_costs_f32"
+    if key not in _fns:
+        lib = ctypes.CDLL(str(LIB))
+        fn = lib.tmo_sqeuclidean_costs_f32
+        fn.restype = None
+        fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int,
+                       ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+        _fns[key] = fn
+    xa = np.ascontiguousarray(np.asarray(x, dtype=np.float32))
+    ya = np.ascontiguousarray(np.asarray(y, dtype=np.float32))
+    if xa.ndim != 3 or ya.ndim != 3 or xa.shape[0] != ya.shape[0] or xa.shape[2] != ya.shape[2]:
+        raise ValueError("x must be (B, N, D) and y (B, M, D)")
+    b, n, d = xa.shape
+    m = ya.shape[1]
+    out = np.empty((b, n, m), dtype=np.float32)
+    _fns[key](xa.ctypes.data, ya.ctypes.data, b, n, m, d, out.ctypes.data)
+    return out
+
+
+def jonker_sqeuclidean_batch(x, y, threads: int = 0) -> np.ndarray:
+    """Oracle of the fused op: the restated producer, then jonker_dense_batch."""
+    return jonker_dense_batch(sqeuclidean_costs(x, y), threads)

@@ -422,3 +422,28 @@ int tmo_jonker_compact_batch_f32(const float *costs, int64_t B, int N, int M,
                                  int64_t *out, int nthreads) {
     return batch_driver(costs, B, N, M, out, nthreads, 1);
 }
+
+/* Squared-Euclidean costs of two point sets, the producer restated by the
+ * fused entry point: costs[b][i][j] = sum over d = 0 .. D-1, in that order,
+ * of (x[b][i][d] - y[b][j][d])^2 in fp32, each operation rounded on its own
+ * (this file builds with -ffp-contract=off), starting from 0.  The order is
+ * that of the reference's lazy sqeuclidean costs
+ * (transport/matrix/cpu/exact/network_simplex_simple.h:453-457), in fp32. */
+void tmo_sqeuclidean_costs_f32(const float *x, const float *y, int64_t B, int N, int M, int D,
+                               float *costs) {
+    for (int64_t b = 0; b < B; ++b) {
+        const float *xb = x + b * (int64_t)N * D;
+        const float *yb = y + b * (int64_t)M * D;
+        float *cb = costs + b * (int64_t)N * M;
+        for (int i = 0; i < N; ++i)
+            for (int j = 0; j < M; ++j) {
+                float acc = 0.0f;
+                for (int d = 0; d < D; ++d) {
+                    const float df = xb[(int64_t)i * D + d] - yb[(int64_t)j * D + d];
+                    const float sq = df * df;
+                    acc = acc + sq;
+                }
+                cb[(int64_t)i * M + j] = acc;
+            }
+    }
+}

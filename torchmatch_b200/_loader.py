@@ -37,6 +37,10 @@ OP_COMPACT = "assignment::jonker_compact_batch"
 OP_COMPACT_UNPACKED = "assignment::jonker_compact_batch_unpacked"
 SCHEMA_UNPACKED = "(Tensor costs) -> (Tensor, Tensor, Tensor, Tensor)"
 
+# fused squared-Euclidean costs; no counterpart op in the reference
+OP_POINTS = "assignment::jonker_sqeuclidean_batch"
+SCHEMA_POINTS = "(Tensor x, Tensor y) -> Tensor"
+
 _LIB_HANDLES: list[object] = []
 
 
@@ -64,6 +68,11 @@ def _fake_unpacked(costs: torch.Tensor):
     )
 
 
+def _fake_points(x: torch.Tensor, y: torch.Tensor) -> torch.Tensor:
+    torch._check(x.dim() == 3 and y.dim() == 3, lambda: "x must be (B, N, D) and y (B, M, D)")
+    return x.new_empty(x.size(0), x.size(1), dtype=torch.long)
+
+
 def _fake_async(costs: torch.Tensor):
     torch._check(costs.dim() == 3, lambda: "costs must be 3D (B, N, M)")
     return (costs.new_empty(costs.size(0), costs.size(1), dtype=torch.long),
@@ -80,7 +89,8 @@ def load() -> None:
     for name, schema, fake in ((OP, SCHEMA, _fake), (OP_UNPACKED, SCHEMA_UNPACKED, _fake_unpacked),
                                (OP_ASYNC, SCHEMA_ASYNC, _fake_async),
                                (OP_COMPACT, SCHEMA, _fake),
-                               (OP_COMPACT_UNPACKED, SCHEMA_UNPACKED, _fake_unpacked)):
+                               (OP_COMPACT_UNPACKED, SCHEMA_UNPACKED, _fake_unpacked),
+                               (OP_POINTS, SCHEMA_POINTS, _fake_points)):
         if not _has_op(name):
             lib = torch.library.Library("assignment", "FRAGMENT")
             lib.define(name.split("::")[1] + schema)

@@ -18,9 +18,12 @@ jonker_dense_batch_async = _OPS.jonker_dense_batch_async
 
 jonker_compact_batch = _OPS.jonker_compact_batch
 jonker_compact_batch_unpacked = _OPS.jonker_compact_batch_unpacked
+# fused squared-Euclidean costs from two point sets (x (B, N, D), y (B, M, D))
+jonker_sqeuclidean_batch = _OPS.jonker_sqeuclidean_batch
 
 __all__ = ["jonker_compact_batch", "jonker_compact_batch_unpacked", "jonker_dense_batch",
-           "jonker_dense_batch_async", "jonker_dense_batch_unpacked"]
+           "jonker_dense_batch_async", "jonker_dense_batch_unpacked",
+           "jonker_sqeuclidean_batch"]
 
 for _name in (
     "jonker_scalar", "jonker_dense", "jonker_compact",

@@ -335,10 +335,12 @@ __device__ __forceinline__ void load_row(const float *__restrict__ src, int i, i
 // load per coordinate).  Partial sums of later coordinate chunks are added to
 // the stored value, which keeps the summation order.  +inf cells become the
 // sentinel when the batch needs it (sanitize).  `dst` has row stride M.
+// kCols columns per lane and pass (2 where the kernel's register cap is 64).
+template <int kCols>
 __device__ void fill_points(float *dst, const float *__restrict__ x,
                             const float *__restrict__ y, int N, int M, int D, int lane,
                             bool sanitize, float sentinel) {
-    constexpr int kCols = 4, kDims = 8;
+    constexpr int kDims = 8;
     const int dend = D > 0 ? D : 1;  // D == 0: one pass that stores zeros
     for (int j0 = 0; j0 < M; j0 += 32 * kCols) {
         for (int d0 = 0; d0 < dend; d0 += kDims) {
@@ -1201,13 +1203,13 @@ __global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ?
             // streaming shape, fused costs: build the problem in this warp's slab
             static_assert(!TILE, "points in TILE mode use the shared-memory tile");
             float *slab = P.slab + ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * P.slab_floats;
-            fill_points(slab, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D, P.N,
+            fill_points<(S > 4) ? 4 : 2>(slab, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D, P.N,
                         P.M, P.D, lane, P.sanitize != 0, P.sentinel);
             __syncwarp();  // orders the lanes' slab stores before the row reads
             src = slab;
         } else if (TILE && P.px) {
             // TILE shape, fused costs: build the problem in the tile itself
-            fill_points(w.tile, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D,
+            fill_points<4>(w.tile, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D,
                         P.N, P.M, P.D, lane, P.sanitize != 0, P.sentinel);
             __syncwarp();
             src = w.tile;
@@ -1357,6 +1359,8 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     if (wpb < 1) return TM_ERR_TOO_LARGE;
     const int64_t need_warps = P.B;
     if ((int64_t)wpb > need_warps) wpb = (int)need_warps;
+    if (PTS && (int64_t)wpb > P.slab_warps) wpb = (int)P.slab_warps;  // one slab per warp
+    if (wpb < 1) return TM_ERR_ARG;
     const int smem = wpb * warp_bytes;
     auto kern = jv_batch_kernel<S, VEC, TILE, FULL, PTS>;
     // The shared-memory opt-in and the occupancy query run once per device
@@ -1388,11 +1392,8 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     int64_t blocks = (P.B + wpb - 1) / wpb;
     const int64_t resident = (int64_t)num_sms() * per_sm;
     if (blocks > resident) blocks = resident;
-    if (PTS) {
-        // one slab per resident warp: fewer slabs, fewer blocks
-        if (P.slab_warps < wpb) return TM_ERR_ARG;
-        if (blocks * wpb > P.slab_warps) blocks = P.slab_warps / wpb;
-    }
+    // one slab per resident warp: fewer slabs, fewer blocks
+    if (PTS && blocks * wpb > P.slab_warps) blocks = P.slab_warps / wpb;
     kern<<<(unsigned)blocks, wpb * 32, smem, stream>>>(P);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);

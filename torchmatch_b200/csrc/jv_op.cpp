@@ -23,6 +23,7 @@
 #include <cuda_runtime.h>
 
 #include <cstddef>
+#include <cstdint>
 
 #include "torchmatch_b200.h"
 
@@ -173,9 +174,53 @@ std::tuple<at::Tensor, at::Tensor> jonker_dense_batch_async_cuda(const at::Tenso
     return {out, status.clone()};
 }
 
+// jonker_sqeuclidean_batch(x (B, N, D), y (B, M, D)) -> (B, N) int64: the
+// mapping of jonker_dense_batch on the squared-Euclidean costs of the two
+// point sets, built inside the solve kernel instead of as a (B, N, M)
+// tensor.  No counterpart op in the reference; the result equals
+// jonker_dense_batch on the costs of a sequential fp32 producer (see the
+// C ABI declaration).
+at::Tensor jonker_sqeuclidean_batch_cuda(const at::Tensor &x, const at::Tensor &y) {
+    TORCH_CHECK(x.is_cuda() && y.is_cuda(), "x and y must be CUDA tensors");
+    TORCH_CHECK(x.device() == y.device(), "x and y must be on the same device");
+    TORCH_CHECK(x.dim() == 3 && y.dim() == 3, "x must be (B, N, D) and y (B, M, D)");
+    TORCH_CHECK(x.size(0) == y.size(0) && x.size(2) == y.size(2),
+                "x (B, N, D) and y (B, M, D) must agree in B and D, got ", x.sizes(), " and ",
+                y.sizes());
+    TORCH_CHECK(x.scalar_type() == at::kFloat || x.scalar_type() == at::kDouble,
+                "x must be float32 or float64, got ", x.scalar_type());
+    TORCH_CHECK(y.scalar_type() == at::kFloat || y.scalar_type() == at::kDouble,
+                "y must be float32 or float64, got ", y.scalar_type());
+    const c10::cuda::CUDAGuard guard(x.device());
+    const int64_t B = x.size(0), N = x.size(1), M = y.size(1), D = x.size(2);
+    if (B == 0 || N == 0 || M == 0)
+        return at::full({B, N}, -1, x.options().dtype(at::kLong));
+    const int64_t K = std::max(N, M);
+    TORCH_CHECK(K <= tm_jv_max_k(), "Batched JV (CUDA) supports max(N, M) <= ", tm_jv_max_k(),
+                ", got K=", K);
+    TORCH_CHECK(D <= INT32_MAX, "D too large");
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+    check_not_capturing(stream, "jonker_sqeuclidean_batch");
+    const at::Tensor xc = x.to(at::kFloat).contiguous(), yc = y.to(at::kFloat).contiguous();
+    const size_t ws_bytes = tm_jv_points_workspace_bytes(B, static_cast<int>(N),
+                                                         static_cast<int>(M));
+    // the caching allocator returns 512-byte aligned blocks
+    at::Tensor scratch = at::empty({(int64_t)ws_bytes}, xc.options().dtype(at::kByte));
+    at::Tensor out = at::empty({B, N}, x.options().dtype(at::kLong));
+    const int rc = tm_jonker_sqeuclidean_batch_f32(
+        xc.const_data_ptr<float>(), yc.const_data_ptr<float>(), B, static_cast<int>(N),
+        static_cast<int>(M), static_cast<int>(D), out.mutable_data_ptr<int64_t>(),
+        scratch.mutable_data_ptr(), ws_bytes, reinterpret_cast<tm_stream_t>(stream));
+    TORCH_CHECK(rc != TM_ERR_NAN, "jonker_sqeuclidean_batch: ", tm_status_string(rc));
+    TORCH_CHECK(rc != TM_ERR_NEG_INF, "jonker_sqeuclidean_batch: ", tm_status_string(rc));
+    TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
+    return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY_IMPL(assignment, CUDA, m) {
+    m.impl("jonker_sqeuclidean_batch", &jonker_sqeuclidean_batch_cuda);
     m.impl("jonker_dense_batch_async", &jonker_dense_batch_async_cuda);
     m.impl("jonker_dense_batch", &jonker_dense_batch_cuda);
     m.impl("jonker_dense_batch_unpacked", &jonker_dense_batch_unpacked_cuda);
