@@ -83,6 +83,7 @@ struct Params {
     // fused squared-Euclidean costs: x (B, N, D) and y (B, M, D) replace
     // `costs`; streaming shapes give each resident warp a slab of N * M
     // floats at slab + (global warp index) * slab_floats
+    int points;          // costs come from x / y (px, py may be null when D == 0)
     const float *px;
     const float *py;
     int D;
@@ -330,23 +331,22 @@ __device__ __forceinline__ void load_row(const float *__restrict__ src, int i, i
 // the reference's lazy costs (transport/matrix/cpu/exact/
 // network_simplex_simple.h:453-457) in single precision, so the solve sees
 // exactly the matrix that a sequential fp32 producer would have written.
-// Each lane owns columns lane + 32 t; their points are held in registers 8
-// coordinates at a time while the rows stream past (x row: one broadcast
-// load per coordinate).  Partial sums of later coordinate chunks are added to
-// the stored value, which keeps the summation order.  +inf cells become the
-// sentinel when the batch needs it (sanitize).  `dst` has row stride M.
-// kCols columns per lane and pass (2 where the kernel's register cap is 64).
+// Each lane owns kCols columns (lane + 32 t) per pass and accumulates their
+// cells of one row in registers over all of D, then stores each cell once;
+// the rows stream past with one broadcast load per coordinate of x.  With
+// D <= 16 the lane's y points stay in registers for the whole pass;
+// otherwise each 16-coordinate chunk is reloaded per row (L1-resident).
+// +inf cells become the sentinel when the batch needs it (sanitize).  `dst`
+// has row stride M.
 template <int kCols>
 __device__ void fill_points(float *dst, const float *__restrict__ x,
                             const float *__restrict__ y, int N, int M, int D, int lane,
                             bool sanitize, float sentinel) {
-    constexpr int kDims = 8;
-    const int dend = D > 0 ? D : 1;  // D == 0: one pass that stores zeros
+    constexpr int kDims = 16;
+    const bool resident = D <= kDims;
     for (int j0 = 0; j0 < M; j0 += 32 * kCols) {
-        for (int d0 = 0; d0 < dend; d0 += kDims) {
-            const int dn = D - d0 < kDims ? D - d0 : kDims;
-            const bool last = d0 + kDims >= dend;
-            float yv[kCols][kDims];
+        float yv[kCols][kDims];
+        auto load_y = [&](int d0, int dn) {
 #pragma unroll
             for (int t = 0; t < kCols; ++t) {
                 const int j = j0 + t * 32 + lane;
@@ -354,27 +354,32 @@ __device__ void fill_points(float *dst, const float *__restrict__ x,
                 for (int e = 0; e < kDims; ++e)
                     yv[t][e] = (j < M && e < dn) ? __ldg(y + (int64_t)j * D + d0 + e) : 0.0f;
             }
-            for (int i = 0; i < N; ++i) {
-                float xv[kDims];
+        };
+        if (resident) load_y(0, D);
+        for (int i = 0; i < N; ++i) {
+            float acc[kCols];
+#pragma unroll
+            for (int t = 0; t < kCols; ++t) acc[t] = 0.0f;
+            for (int d0 = 0; d0 < D; d0 += kDims) {
+                const int dn = D - d0 < kDims ? D - d0 : kDims;
+                if (!resident) load_y(d0, dn);
+                const float *xr = x + (int64_t)i * D + d0;
 #pragma unroll
                 for (int e = 0; e < kDims; ++e)
-                    xv[e] = e < dn ? __ldg(x + (int64_t)i * D + d0 + e) : 0.0f;
-                float *row = dst + (int64_t)i * M;
+                    if (e < dn) {
+                        const float xe = __ldg(xr + e);
 #pragma unroll
-                for (int t = 0; t < kCols; ++t) {
-                    const int j = j0 + t * 32 + lane;
-                    if (j < M) {
-                        float acc = d0 == 0 ? 0.0f : row[j];
-#pragma unroll
-                        for (int e = 0; e < kDims; ++e)
-                            if (e < dn) {
-                                const float df = __fsub_rn(xv[e], yv[t][e]);
-                                acc = __fadd_rn(acc, __fmul_rn(df, df));
-                            }
-                        if (last && sanitize && isinf(acc)) acc = sentinel;
-                        row[j] = acc;
+                        for (int t = 0; t < kCols; ++t) {
+                            const float df = __fsub_rn(xe, yv[t][e]);
+                            acc[t] = __fadd_rn(acc[t], __fmul_rn(df, df));
+                        }
                     }
-                }
+            }
+            float *row = dst + (int64_t)i * M;
+#pragma unroll
+            for (int t = 0; t < kCols; ++t) {
+                const int j = j0 + t * 32 + lane;
+                if (j < M) row[j] = (sanitize && isinf(acc[t])) ? sentinel : acc[t];
             }
         }
     }
@@ -1152,7 +1157,7 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
 
 // ------------------------------------------------------------------ kernel
 template <int S, int VEC, bool TILE, bool FULL, bool PTS>
-__global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ? 1 : 4) jv_batch_kernel(const Params P0) {
+__global__ void __launch_bounds__((TILE || S > 4 || PTS) ? 512 : 256, (TILE || S > 4 || PTS) ? 1 : 4) jv_batch_kernel(const Params P0) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     Params P = P0;
@@ -1199,20 +1204,19 @@ __global__ void __launch_bounds__((TILE || S > 4) ? 512 : 256, (TILE || S > 4) ?
         const float *g = P.costs + b * per;
         const float *src = g;
         TMJV_T(t_load);
-        if constexpr (PTS) {
-            // streaming shape, fused costs: build the problem in this warp's slab
-            static_assert(!TILE, "points in TILE mode use the shared-memory tile");
+        if constexpr (PTS && TILE) {
+            // fused costs, TILE shape: build the problem in the tile itself
+            fill_points<2>(w.tile, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D,
+                           P.N, P.M, P.D, lane, P.sanitize != 0, P.sentinel);
+            __syncwarp();
+            src = w.tile;
+        } else if constexpr (PTS) {
+            // fused costs, streaming shape: build the problem in this warp's slab
             float *slab = P.slab + ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * P.slab_floats;
-            fill_points<(S > 4) ? 4 : 2>(slab, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D, P.N,
+            fill_points<2>(slab, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D, P.N,
                         P.M, P.D, lane, P.sanitize != 0, P.sentinel);
             __syncwarp();  // orders the lanes' slab stores before the row reads
             src = slab;
-        } else if (TILE && P.px) {
-            // TILE shape, fused costs: build the problem in the tile itself
-            fill_points<4>(w.tile, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D,
-                        P.N, P.M, P.D, lane, P.sanitize != 0, P.sentinel);
-            __syncwarp();
-            src = w.tile;
         } else if constexpr (TILE) {
             bool ok = true;
             if (P.bulk_ok) {
@@ -1355,7 +1359,8 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     P.warp_bytes = warp_bytes;
     P.tile_floats = tile_floats;
     int wpb = kSmemLimit / warp_bytes;
-    if (wpb > ((TILE || S > 4) ? kMaxWarpsPerBlock : 8)) wpb = (TILE || S > 4) ? kMaxWarpsPerBlock : 8;
+    const int wcap = (TILE || S > 4 || PTS) ? kMaxWarpsPerBlock : 8;
+    if (wpb > wcap) wpb = wcap;
     if (wpb < 1) return TM_ERR_TOO_LARGE;
     const int64_t need_warps = P.B;
     if ((int64_t)wpb > need_warps) wpb = (int)need_warps;
@@ -1420,7 +1425,19 @@ static int launch(Params P, cudaStream_t stream) {
 #define TM_F(SS, VV)                                                                     \
     return tile ? launch_t<SS, VV, true, true>(P, stream)                                \
                 : launch_t<SS, VV, false, true>(P, stream)
-    if (P.px && !tile) {
+    if (P.points && tile) {
+        // fused costs, TILE shape: rows come from the tile the kernel fills
+#define TM_P(SS, VV, FF) return launch_t<SS, VV, true, FF, true>(P, stream)
+        switch (S) {
+        case 1: if (full) { TM_P(1, 1, true); } TM_P(1, 1, false);
+        case 2: if (full) { TM_P(2, 2, true); } TM_P(2, 1, false);
+        case 3: TM_P(3, 1, false);
+        case 4: if (full) { TM_P(4, 4, true); } TM_P(4, 1, false);
+        default: return TM_ERR_ARG;  // wider problems never fit the tile
+        }
+#undef TM_P
+    }
+    if (P.points) {
         // fused costs, streaming shape: rows come from the warp slabs, which
         // are 256-byte aligned with row stride M
         const bool s4 = P.M % 4 == 0;
@@ -1479,10 +1496,10 @@ static int64_t points_slabs(int64_t B, int N, int M) {
     if (tile_bytes * tile_min_warps() <= kSmemLimit || B <= 0) return 0;
     const int warp_bytes = (book_bytes(32 * S, true) + 127) & ~127;
     int wpb = kSmemLimit / warp_bytes;
-    const int cap = S > 4 ? kMaxWarpsPerBlock : 8;
-    if (wpb > cap) wpb = cap;
+    // the slab kernels launch like the wide ones: up to 16 warps, one block per SM
+    if (wpb > kMaxWarpsPerBlock) wpb = kMaxWarpsPerBlock;
     if ((int64_t)wpb > B) wpb = (int)B;
-    int per_sm = S > 4 ? 1 : 4;
+    int per_sm = 1;
     const int fit = (228 * 1024) / (wpb * warp_bytes);
     if (fit < per_sm) per_sm = fit > 0 ? fit : 1;
     int64_t blocks = (B + wpb - 1) / wpb;
@@ -1607,6 +1624,7 @@ static int solve_impl(const float *costs, int64_t B, int N, int M, float sentine
     P.status = &ws->status;
     P.ticket = &ws->ticket;
     if (pts) {
+        P.points = 1;
         P.px = pts->x;
         P.py = pts->y;
         P.D = pts->D;
