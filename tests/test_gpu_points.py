@@ -47,6 +47,9 @@ SHAPES = [
     (40, 200, 256, 16),   # slabs, S = 8, rectangular, vector loads
     (48, 256, 256, 16),   # slabs, S = 8, square (config-5 shape)
     (24, 256, 255, 33),   # slabs, S = 8, scalar loads, D with a ragged chunk
+    (32, 256, 256, 32),   # slabs, blocked producer over two coordinate chunks
+    (128, 64, 64, 32),    # tile, blocked producer over two coordinate chunks
+    (64, 45, 37, 16),     # tile, blocked producer with a partial row block
     (32, 40, 40, 1),
     (16, 24, 30, 0),      # D = 0: every cost is 0
 ]

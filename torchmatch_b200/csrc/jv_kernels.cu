@@ -385,6 +385,83 @@ __device__ void fill_points(float *dst, const float *__restrict__ x,
     }
 }
 
+// The same cells for D a multiple of 16, latency-hidden: rows go in blocks
+// of 8, and one block's x coordinates (one 16-coordinate chunk) arrive with
+// 4 independent coalesced loads per lane -- lane l of load k holds
+// coordinate l % 16 of row 2k + l / 16 -- and reach every lane by shuffles,
+// instead of one dependent L2 round trip per row.  An 8-row x kCols block of
+// sums stays in registers over all chunks, in coordinate order, so each cell
+// is still the sequential fp32 sum and is stored once.
+template <int kCols>
+__device__ void fill_points16(float *dst, const float *__restrict__ x,
+                              const float *__restrict__ y, int N, int M, int D, int lane,
+                              bool sanitize, float sentinel) {
+    constexpr int kRows = 8, kDims = 16;
+    for (int j0 = 0; j0 < M; j0 += 32 * kCols) {
+        float yv[kCols][kDims];
+        for (int i0 = 0; i0 < N; i0 += kRows) {
+            float acc[kRows][kCols];
+#pragma unroll
+            for (int r = 0; r < kRows; ++r)
+#pragma unroll
+                for (int t = 0; t < kCols; ++t) acc[r][t] = 0.0f;
+            for (int d0 = 0; d0 < D; d0 += kDims) {
+                if (d0 > 0 || i0 == 0 || D > kDims) {
+#pragma unroll
+                    for (int t = 0; t < kCols; ++t) {
+                        const int j = j0 + t * 32 + lane;
+#pragma unroll
+                        for (int e = 0; e < kDims; ++e)
+                            yv[t][e] = j < M ? __ldg(y + (int64_t)j * D + d0 + e) : 0.0f;
+                    }
+                }
+                float xs[kRows / 2];
+#pragma unroll
+                for (int k = 0; k < kRows / 2; ++k) {
+                    const int r = i0 + 2 * k + (lane >> 4);
+                    xs[k] = r < N ? __ldg(x + (int64_t)r * D + d0 + (lane & 15)) : 0.0f;
+                }
+#pragma unroll
+                for (int k = 0; k < kRows / 2; ++k)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int e = 0; e < kDims; ++e) {
+                            const float xe = __shfl_sync(kFull, xs[k], h * 16 + e);
+#pragma unroll
+                            for (int t = 0; t < kCols; ++t) {
+                                const float df = __fsub_rn(xe, yv[t][e]);
+                                acc[2 * k + h][t] = __fadd_rn(acc[2 * k + h][t], __fmul_rn(df, df));
+                            }
+                        }
+            }
+#pragma unroll
+            for (int r = 0; r < kRows; ++r) {
+                if (i0 + r < N) {
+                    float *row = dst + (int64_t)(i0 + r) * M;
+#pragma unroll
+                    for (int t = 0; t < kCols; ++t) {
+                        const int j = j0 + t * 32 + lane;
+                        if (j < M)
+                            row[j] = (sanitize && isinf(acc[r][t])) ? sentinel : acc[r][t];
+                    }
+                }
+            }
+        }
+    }
+}
+
+// Producer dispatch: the blocked form for D a positive multiple of 16.
+template <int kCols>
+__device__ __forceinline__ void fill_cells(float *dst, const float *__restrict__ x,
+                                           const float *__restrict__ y, int N, int M, int D,
+                                           int lane, bool sanitize, float sentinel) {
+    if (D > 0 && D % 16 == 0)
+        fill_points16<kCols>(dst, x, y, N, M, D, lane, sanitize, sentinel);
+    else
+        fill_points<kCols>(dst, x, y, N, M, D, lane, sanitize, sentinel);
+}
+
 // Writes one problem's result: the packed row -> column mapping (column >= M
 // or unsolved -> -1, cpu/ops.cpp:274-283) and, when requested, the compacted
 // form of jonker_dense_batch_unpacked (cpu/ops.cpp:378-414): matched pairs in
@@ -1206,14 +1283,14 @@ __global__ void __launch_bounds__((TILE || S > 4 || PTS) ? 512 : 256, (TILE || S
         TMJV_T(t_load);
         if constexpr (PTS && TILE) {
             // fused costs, TILE shape: build the problem in the tile itself
-            fill_points<2>(w.tile, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D,
+            fill_cells<2>(w.tile, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D,
                            P.N, P.M, P.D, lane, P.sanitize != 0, P.sentinel);
             __syncwarp();
             src = w.tile;
         } else if constexpr (PTS) {
             // fused costs, streaming shape: build the problem in this warp's slab
             float *slab = P.slab + ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * P.slab_floats;
-            fill_points<2>(slab, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D, P.N,
+            fill_cells<(S > 6) ? 1 : 2>(slab, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D, P.N,
                         P.M, P.D, lane, P.sanitize != 0, P.sentinel);
             __syncwarp();  // orders the lanes' slab stores before the row reads
             src = slab;
@@ -1364,7 +1441,7 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     if (wpb < 1) return TM_ERR_TOO_LARGE;
     const int64_t need_warps = P.B;
     if ((int64_t)wpb > need_warps) wpb = (int)need_warps;
-    if (PTS && (int64_t)wpb > P.slab_warps) wpb = (int)P.slab_warps;  // one slab per warp
+    if (PTS && !TILE && (int64_t)wpb > P.slab_warps) wpb = (int)P.slab_warps;  // one slab per warp
     if (wpb < 1) return TM_ERR_ARG;
     const int smem = wpb * warp_bytes;
     auto kern = jv_batch_kernel<S, VEC, TILE, FULL, PTS>;
@@ -1398,7 +1475,7 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     const int64_t resident = (int64_t)num_sms() * per_sm;
     if (blocks > resident) blocks = resident;
     // one slab per resident warp: fewer slabs, fewer blocks
-    if (PTS && blocks * wpb > P.slab_warps) blocks = P.slab_warps / wpb;
+    if (PTS && !TILE && blocks * wpb > P.slab_warps) blocks = P.slab_warps / wpb;
     kern<<<(unsigned)blocks, wpb * 32, smem, stream>>>(P);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
