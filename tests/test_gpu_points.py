@@ -43,13 +43,17 @@ SHAPES = [
     (512, 64, 64, 16),    # tile, config-2 shape
     (256, 100, 150, 8),   # tile, rectangular
     (96, 128, 128, 16),   # slabs, S = 4, square, vector loads
-    (64, 130, 97, 3),     # slabs, S = 5, rectangular, scalar loads
+    (64, 130, 97, 3),     # tile at S = 5, generic producer
+    (64, 200, 150, 3),    # slabs, S = 7, rectangular, scalar loads
     (40, 200, 256, 16),   # slabs, S = 8, rectangular, vector loads
     (48, 256, 256, 16),   # slabs, S = 8, square (config-5 shape)
     (24, 256, 255, 33),   # slabs, S = 8, scalar loads, D with a ragged chunk
     (32, 256, 256, 32),   # slabs, blocked producer over two coordinate chunks
     (128, 64, 64, 32),    # tile, blocked producer over two coordinate chunks
     (64, 45, 37, 16),     # tile, blocked producer with a partial row block
+    (64, 130, 97, 16),    # tile at S = 5 (rectangular), blocked producer
+    (64, 8, 250, 16),     # tile at S = 8 (few rows, wide)
+    (32, 180, 60, 7),     # tile at S = 6, generic producer
     (32, 40, 40, 1),
     (16, 24, 30, 0),      # D = 0: every cost is 0
 ]
@@ -166,3 +170,16 @@ def test_c_abi_small_workspace_and_arguments(oracle_mod):
                                                stream) == 5
     # shapes solved in the tile need only the 256-byte header
     assert lib.tm_jv_points_workspace_bytes(64, 64, 64) == 256
+
+
+@pytest.mark.parametrize("d", [5, 16])
+def test_shape_sweep(ops, oracle_mod, d):
+    # every slot count, square and rectangular, tile and slab storage
+    g = torch.Generator().manual_seed(d)
+    for k in range(1, 257, 17):
+        for n, m in ((k, k), (k, max(1, k // 2 + 3)), (max(1, k // 3), k)):
+            x = torch.randn(6, n, d, generator=g)
+            y = torch.randn(6, m, d, generator=g)
+            got = ops.jonker_sqeuclidean_batch(x.cuda(), y.cuda()).cpu().numpy()
+            np.testing.assert_array_equal(got, oracle_mod.jonker_sqeuclidean_batch(x, y),
+                                          err_msg=f"n={n} m={m} d={d}")
