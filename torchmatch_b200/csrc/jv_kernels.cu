@@ -237,13 +237,11 @@ __device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP,
 // +inf cells become the sentinel here; in TILE mode the tile was already
 // sanitised.
 // Read-only loads of the input batch go through the non-coherent path.  Rows
-// of a points slab (PTS) were written earlier in the same launch by the same
-// warp, which that path does not allow, so they are read with ordinary
-// (weak, L1-cached) loads; the warp's __syncwarp after the slab stores orders
-// them before these reads.
+// of a points slab (PTS) were written earlier in the same launch, which that
+// path does not allow, so they are read with L2-only loads instead.
 template <bool PTS, class T>
 __device__ __forceinline__ T gload(const T *p) {
-    if constexpr (PTS) return __ldca(p);
+    if constexpr (PTS) return __ldcg(p);
     else return __ldg(p);
 }
 
@@ -387,52 +385,34 @@ __device__ void fill_points(float *dst, const float *__restrict__ x,
     }
 }
 
-// Packed pairs of fp32 (sm_100 f32x2 arithmetic): each half is one IEEE
-// fp32 operation with round-to-nearest, exactly like the scalar form.
-__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void unpack2(unsigned long long v, float &lo, float &hi) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-// acc + (x - y)^2 on both halves, each step rounded on its own
-__device__ __forceinline__ unsigned long long sqacc2(unsigned long long acc, unsigned long long x,
-                                                     unsigned long long y) {
-    unsigned long long d, q;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(x), "l"(y));
-    asm("mul.rn.f32x2 %0, %1, %1;" : "=l"(q) : "l"(d));
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(acc) : "l"(acc), "l"(q));
-    return acc;
-}
-
 // The same cells for D a multiple of 16, latency-hidden: rows go in blocks
 // of 8, and one block's x coordinates (one 16-coordinate chunk) arrive with
 // 4 independent coalesced loads per lane -- lane l of load k holds
 // coordinate l % 16 of row 2k + l / 16 -- and reach every lane by shuffles,
-// instead of one dependent L2 round trip per row.  Each lane owns one column
-// per pass; the sums of an 8-row block stay in registers over all chunks, in
-// coordinate order, so each cell is still the sequential fp32 sum and is
-// stored once.  The arithmetic runs on packed pairs: the two rows of one
-// load against the column's coordinate in both halves.
+// instead of one dependent L2 round trip per row.  An 8-row x kCols block of
+// sums stays in registers over all chunks, in coordinate order, so each cell
+// is still the sequential fp32 sum and is stored once.
+template <int kCols>
 __device__ void fill_points16(float *dst, const float *__restrict__ x,
                               const float *__restrict__ y, int N, int M, int D, int lane,
                               bool sanitize, float sentinel) {
     constexpr int kRows = 8, kDims = 16;
-    for (int j0 = 0; j0 < M; j0 += 32) {
-        const int j = j0 + lane;
-        unsigned long long yy[kDims];  // (y_j, y_j) per coordinate of the chunk
+    for (int j0 = 0; j0 < M; j0 += 32 * kCols) {
+        float yv[kCols][kDims];
         for (int i0 = 0; i0 < N; i0 += kRows) {
-            unsigned long long acc[kRows / 2];  // rows (i0 + 2k, i0 + 2k + 1)
+            float acc[kRows][kCols];
 #pragma unroll
-            for (int k = 0; k < kRows / 2; ++k) acc[k] = 0ull;
+            for (int r = 0; r < kRows; ++r)
+#pragma unroll
+                for (int t = 0; t < kCols; ++t) acc[r][t] = 0.0f;
             for (int d0 = 0; d0 < D; d0 += kDims) {
                 if (d0 > 0 || i0 == 0 || D > kDims) {
 #pragma unroll
-                    for (int e = 0; e < kDims; ++e) {
-                        const float yj = j < M ? __ldg(y + (int64_t)j * D + d0 + e) : 0.0f;
-                        yy[e] = pack2(yj, yj);
+                    for (int t = 0; t < kCols; ++t) {
+                        const int j = j0 + t * 32 + lane;
+#pragma unroll
+                        for (int e = 0; e < kDims; ++e)
+                            yv[t][e] = j < M ? __ldg(y + (int64_t)j * D + d0 + e) : 0.0f;
                     }
                 }
                 float xs[kRows / 2];
@@ -444,22 +424,26 @@ __device__ void fill_points16(float *dst, const float *__restrict__ x,
 #pragma unroll
                 for (int k = 0; k < kRows / 2; ++k)
 #pragma unroll
-                    for (int e = 0; e < kDims; ++e) {
-                        const float x0 = __shfl_sync(kFull, xs[k], e);
-                        const float x1 = __shfl_sync(kFull, xs[k], 16 + e);
-                        acc[k] = sqacc2(acc[k], pack2(x0, x1), yy[e]);
-                    }
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int e = 0; e < kDims; ++e) {
+                            const float xe = __shfl_sync(kFull, xs[k], h * 16 + e);
+#pragma unroll
+                            for (int t = 0; t < kCols; ++t) {
+                                const float df = __fsub_rn(xe, yv[t][e]);
+                                acc[2 * k + h][t] = __fadd_rn(acc[2 * k + h][t], __fmul_rn(df, df));
+                            }
+                        }
             }
-            if (j < M) {
 #pragma unroll
-                for (int k = 0; k < kRows / 2; ++k) {
-                    float c[2];
-                    unpack2(acc[k], c[0], c[1]);
+            for (int r = 0; r < kRows; ++r) {
+                if (i0 + r < N) {
+                    float *row = dst + (int64_t)(i0 + r) * M;
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int r = i0 + 2 * k + h;
-                        if (r < N)
-                            dst[(int64_t)r * M + j] = (sanitize && isinf(c[h])) ? sentinel : c[h];
+                    for (int t = 0; t < kCols; ++t) {
+                        const int j = j0 + t * 32 + lane;
+                        if (j < M)
+                            row[j] = (sanitize && isinf(acc[r][t])) ? sentinel : acc[r][t];
                     }
                 }
             }
@@ -473,7 +457,7 @@ __device__ __forceinline__ void fill_cells(float *dst, const float *__restrict__
                                            const float *__restrict__ y, int N, int M, int D,
                                            int lane, bool sanitize, float sentinel) {
     if (D > 0 && D % 16 == 0)
-        fill_points16(dst, x, y, N, M, D, lane, sanitize, sentinel);
+        fill_points16<kCols>(dst, x, y, N, M, D, lane, sanitize, sentinel);
     else
         fill_points<kCols>(dst, x, y, N, M, D, lane, sanitize, sentinel);
 }
