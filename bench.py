@@ -20,8 +20,9 @@ Workloads (synthetic, seeded; tests/golden/cases.py holds the recipes):
 `value` is device time (CUDA events, max over ranks) with inputs resident in
 HBM; consecutive steps rotate over enough input copies that their total
 exceeds twice the 126 MB L2, so every step reads its batch from HBM.  `e2e`
-is the same op with a pinned host batch copied in and the result copied out
-inside each timed step.  `roofline` is measured live: the solve kernel alone,
+is the same op with a pinned host batch copied in (four pieces, double-
+buffered on a copy stream) and the result copied out to pinned memory inside
+each timed step.  `roofline` is measured live: the solve kernel alone,
 launched through the C ABI between CUDA events on its stream, against the
 measured HBM copy bandwidth.  `cpu_baseline` times the reference's own CPU
 solver (oracle/_ref, built from the reference sources) on the host cores.
@@ -350,6 +351,16 @@ def run_ours(args):
     # step k solves (double-buffered), as a user of the op would pipeline it;
     # every copy still lies inside the timed region.
     copy_stream = torch.cuda.Stream(dev)
+    res = torch.empty(eb, n, dtype=torch.long).pin_memory()
+
+    def upload(dst):
+        # four pieces: on this host link one 64 MiB pinned copy ran at
+        # 37.5 GB/s, the same bytes in 2-16 pieces at 53-55 GB/s
+        flat_d, flat_h = dst.view(-1), host.view(-1)
+        step_n = -(-flat_h.numel() // 4)
+        for p0 in range(0, flat_h.numel(), step_n):
+            flat_d[p0:p0 + step_n].copy_(flat_h[p0:p0 + step_n], non_blocking=True)
+
     dbuf = [torch.empty(host.shape, dtype=host.dtype, device=dev) for _ in range(2)]
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
@@ -359,7 +370,7 @@ def run_ours(args):
     e0.record(compute)
     copy_stream.wait_event(e0)
     with torch.cuda.stream(copy_stream):
-        dbuf[0].copy_(host, non_blocking=True)
+        upload(dbuf[0])
         ready[0].record(copy_stream)
     for k in range(e_steps):
         cur, nxt = k % 2, (k + 1) % 2
@@ -367,14 +378,15 @@ def run_ours(args):
             with torch.cuda.stream(copy_stream):
                 if k >= 1:
                     copy_stream.wait_event(free[nxt])
-                dbuf[nxt].copy_(host, non_blocking=True)
+                upload(dbuf[nxt])
                 ready[nxt].record(copy_stream)
         compute.wait_event(ready[cur])
         out_d = step(dbuf[cur])
         free[cur].record(compute)
-        res = out_d.cpu()
+        res.copy_(out_d, non_blocking=True)  # complete at the next step's sync and at e1
     e1.record(compute)
     barrier()
+    assert int(res.min()) >= -1  # the last mapping arrived on the host
     e_ms = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([e_ms], device=dev)
