@@ -344,7 +344,7 @@ def run_ours(args):
     pipelined = None
     if world == 1:
         aop = torch.ops.assignment.jonker_dense_batch_async
-        nstreams = 3
+        nstreams = args.streams
         streams = [torch.cuda.Stream(dev) for _ in range(nstreams)]
 
         def pipe(nsteps):
@@ -593,6 +593,8 @@ def main():
     ap.add_argument("--once", action="store_true",
                     help="solve the workload twice and exit (a small case for ncu captures)")
     ap.add_argument("--batch", type=int, default=0, help="override B (with --once / --fused)")
+    ap.add_argument("--streams", type=int, default=3,
+                    help="streams of the pipelined (async op) measurement")
     ap.add_argument("--fused", action="store_true",
                     help="fused squared-Euclidean cost construction on config-5 point sets")
     args = ap.parse_args()
