@@ -527,14 +527,50 @@ def run_fused(args):
     # the unfused pipeline a user would run: torch builds the cost tensor
     # (cdist, squared; rounds differently, so timing only), then the dense op
     unfused_ms = timed(lambda: ops.jonker_dense_batch(torch.cdist(x, y).pow_(2)), steps)
-    # end to end: pinned host points in, mapping out, every step
+    # end to end: pinned host points in (four pieces each, double-buffered on
+    # a copy stream), mapping out to pinned memory, every step
     hb = min(b, 16384)
     hx, hy = x[:hb].cpu().pin_memory(), y[:hb].cpu().pin_memory()
+    res = torch.empty(hb, n, dtype=torch.long).pin_memory()
+    cs = torch.cuda.Stream(dev)
+    comp = torch.cuda.current_stream(dev)
+    dx = [torch.empty_like(hx, device=dev) for _ in range(2)]
+    dy = [torch.empty_like(hy, device=dev) for _ in range(2)]
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
 
-    def e2e_step():
-        ops.jonker_sqeuclidean_batch(hx.to(dev, non_blocking=True),
-                                     hy.to(dev, non_blocking=True)).cpu()
-    e2e_ms = timed(e2e_step, max(3, steps // 2))
+    def upload(k):
+        with torch.cuda.stream(cs):
+            if k >= 2:
+                cs.wait_event(free[k % 2])
+            for src, dst in ((hx, dx[k % 2]), (hy, dy[k % 2])):
+                fs, fd = src.view(-1), dst.view(-1)
+                q = -(-fs.numel() // 4)
+                for p0 in range(0, fs.numel(), q):
+                    fd[p0:p0 + q].copy_(fs[p0:p0 + q], non_blocking=True)
+            ready[k % 2].record(cs)
+
+    def e2e_run(nsteps):
+        cs.wait_stream(comp)
+        upload(0)
+        for k in range(nsteps):
+            if k + 1 < nsteps:
+                upload(k + 1)
+            comp.wait_event(ready[k % 2])
+            out_k = ops.jonker_sqeuclidean_batch(dx[k % 2], dy[k % 2])
+            free[k % 2].record(comp)
+            res.copy_(out_k, non_blocking=True)
+
+    e2e_run(2)
+    torch.cuda.synchronize()
+    e_steps = max(3, steps // 2)
+    q0 = torch.cuda.Event(enable_timing=True)
+    q1 = torch.cuda.Event(enable_timing=True)
+    q0.record(comp)
+    e2e_run(e_steps)
+    q1.record(comp)
+    torch.cuda.synchronize()
+    e2e_ms = q0.elapsed_time(q1) / e_steps
     peak, peak_src = peak_hbm()
     alg = b * (2 * n * d * 4 + n * 8)
     achieved = alg / (abi_ms / 1e3) / 1e9
