@@ -585,7 +585,9 @@ def run_fused(args):
                    "l2": f"points {2 * b * n * d * 4 / 2**20:.0f} MiB, slabs "
                          f"{nbytes / 2**20:.0f} MiB (> L2)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "traffic": None,
+                     "frac": achieved / peak,
+                     "traffic": int(traffic_for("c5_fused") * b / 65536)
+                     if traffic_for("c5_fused") else None,
                      "kernel": "jv_batch_kernel (points, check mode)",
                      "avg_launch_us": abi_ms * 1e3, "alg_bytes_per_launch": alg,
                      "peak_source": peak_src},

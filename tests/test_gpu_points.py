@@ -183,3 +183,9 @@ def test_shape_sweep(ops, oracle_mod, d):
             got = ops.jonker_sqeuclidean_batch(x.cuda(), y.cuda()).cpu().numpy()
             np.testing.assert_array_equal(got, oracle_mod.jonker_sqeuclidean_batch(x, y),
                                           err_msg=f"n={n} m={m} d={d}")
+
+
+def test_opcheck(ops):
+    x, y = _points(8, 20, 24, 5, seed=9)
+    torch.library.opcheck(ops.jonker_sqeuclidean_batch, (x.cuda(), y.cuda()),
+                          test_utils=("test_schema", "test_faketensor"))
