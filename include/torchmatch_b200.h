@@ -28,7 +28,8 @@
  *                           cpu/jonker_compact_core.h) on the GPU
  *   tm_jonker_dense_batch_async_f32  no host synchronisation (capturable)
  *   tm_jonker_dense_batch_f32_noalloc  no allocation by the caller
- *   tm_jonker_sqeuclidean_batch_f32  squared-Euclidean costs built from two
+ *   tm_jonker_sqeuclidean_batch_f32, tm_jv_points_solve_f32
+ *                           squared-Euclidean costs built from two
  *                           point sets inside the solve kernel (no (B, N, M)
  *                           cost tensor in memory)
  *
@@ -213,6 +214,16 @@ int tm_jonker_compact_batch_unpacked_f32(const float *costs, int64_t B, int N, i
  * TM_ERR_ARG below one slab).  No counterpart op in the reference, whose
  * callers build the cost tensor first (tests/_costgen.py) and pass it. */
 size_t tm_jv_points_workspace_bytes(int64_t B, int N, int M);
+/* One launch of the fused solve, for callers that combine statistics
+ * themselves (e.g. across GPUs): with check != 0 it is the fused form of
+ * tm_jv_solve_checked_f32 (statistics zeroed and gathered into
+ * workspace->stats, problems with non-finite cells left as rows of -1);
+ * with check == 0 the fused form of tm_jv_solve_f32 (`sentinel` replaces
+ * +inf cells when has_pos_inf != 0).  Other arguments as for
+ * tm_jonker_sqeuclidean_batch_f32. */
+int tm_jv_points_solve_f32(const float *x, const float *y, int64_t B, int N, int M, int D,
+                           float sentinel, int has_pos_inf, int check, int64_t *out,
+                           void *workspace, size_t workspace_bytes, tm_stream_t stream);
 int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, int N, int M,
                                     int D, int64_t *out, void *workspace,
                                     size_t workspace_bytes, tm_stream_t stream);

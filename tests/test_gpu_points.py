@@ -189,3 +189,41 @@ def test_opcheck(ops):
     x, y = _points(8, 20, 24, 5, seed=9)
     torch.library.opcheck(ops.jonker_sqeuclidean_batch, (x.cuda(), y.cuda()),
                           test_utils=("test_schema", "test_faketensor"))
+
+
+SHARDED_SCRIPT = """
+import os, sys
+sys.path.insert(0, {root!r}); sys.path.insert(0, {root!r} + "/tests")
+os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT="29541", RANK="0", WORLD_SIZE="1")
+import numpy as np, torch, torch.distributed as dist
+import oracle, torchmatch_b200
+from torchmatch_b200 import sharded
+torch.cuda.set_device(0)
+dist.init_process_group("nccl", device_id=torch.device("cuda", 0))
+g = torch.Generator().manual_seed(31)
+for b, n, m, d, inf in ((64, 64, 64, 16, False), (32, 200, 180, 16, True), (16, 90, 120, 5, True)):
+    x = torch.randn(b, n, d, generator=g); y = torch.randn(b, m, d, generator=g)
+    if inf:
+        x[1, 2, 0] = float("inf")
+    got = sharded.solve_points_sharded(x.cuda(), y.cuda()).cpu().numpy()
+    assert np.array_equal(got, oracle.jonker_sqeuclidean_batch(x, y)), (b, n, m, d)
+x = torch.randn(4, 8, 3, generator=g); x[0, 0, 0] = float("nan")
+try:
+    sharded.solve_points_sharded(x.cuda(), torch.randn(4, 8, 3).cuda())
+    print("NO_RAISE")
+except RuntimeError as e:
+    assert "NaN" in str(e)
+dist.destroy_process_group()
+print("POINTS_SHARDED_OK")
+"""
+
+
+def test_solve_points_sharded_one_rank():
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = str(Path(__file__).resolve().parent.parent)
+    r = subprocess.run([sys.executable, "-c", SHARDED_SCRIPT.format(root=root)],
+                       capture_output=True, text=True, timeout=300)
+    assert "POINTS_SHARDED_OK" in r.stdout, r.stdout[-2000:] + r.stderr[-3000:]

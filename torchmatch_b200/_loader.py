@@ -130,6 +130,9 @@ def core() -> ctypes.CDLL:
     lib.tm_jonker_sqeuclidean_batch_f32.argtypes = [vp, vp, i64, i32, i32, i32, vp, vp,
                                                    ctypes.c_size_t, vp]
     lib.tm_jonker_sqeuclidean_batch_f32.restype = i32
+    lib.tm_jv_points_solve_f32.argtypes = [vp, vp, i64, i32, i32, i32, ctypes.c_float, i32, i32,
+                                          vp, vp, ctypes.c_size_t, vp]
+    lib.tm_jv_points_solve_f32.restype = i32
     lib.tm_jv_debug_set_loop_bound.argtypes = [i32]
     lib.tm_jv_debug_set_loop_bound.restype = None
     lib.tm_status_string.restype = ctypes.c_char_p
@@ -156,6 +159,7 @@ EXPORTED = (
     "tm_jonker_compact_batch_unpacked_f32",
     "tm_jv_points_workspace_bytes",
     "tm_jonker_sqeuclidean_batch_f32",
+    "tm_jv_points_solve_f32",
     "tm_last_cuda_error",
     "tm_jv_debug_set_loop_bound",
     "tm_status_string",

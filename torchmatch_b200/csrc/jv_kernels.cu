@@ -1829,9 +1829,9 @@ size_t tm_jv_points_workspace_bytes(int64_t B, int N, int M) {
            (size_t)tmjv::points_slabs(B, N, M) * (size_t)tmjv::points_slab_floats(N, M) * 4;
 }
 
-int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, int N, int M,
-                                    int D, int64_t *out, void *workspace,
-                                    size_t workspace_bytes, tm_stream_t stream_) {
+int tm_jv_points_solve_f32(const float *x, const float *y, int64_t B, int N, int M, int D,
+                           float sentinel, int has_pos_inf, int check, int64_t *out,
+                           void *workspace, size_t workspace_bytes, tm_stream_t stream_) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (B < 0 || N < 0 || M < 0 || D < 0) return TM_ERR_ARG;
     if (B == 0 || N == 0) return TM_OK;
@@ -1839,7 +1839,8 @@ int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, i
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return TM_ERR_ARG;
     const int K = N > M ? N : M;
     if (K > tm_jv_max_k()) return TM_ERR_TOO_LARGE;
-    if (M == 0) return solve_impl(nullptr, B, N, M, 0.0f, 0, 0, out, workspace, stream_);
+    if (M == 0)
+        return solve_impl(nullptr, B, N, M, 0.0f, 0, check ? 1 : 0, out, workspace, stream_);
     if (D > 0 && (!x || !y)) return TM_ERR_ARG;
     tmjv::StreamDevice scope(stream);
     if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
@@ -1850,10 +1851,27 @@ int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, i
         pts.slab_warps = (int64_t)((workspace_bytes - tmjv::kPointsHeader) / 4) / pts.slab_floats;
         if (pts.slab_warps < 1) return TM_ERR_ARG;
     }
+    return check ? solve_impl(nullptr, B, N, M, 0.0f, 0, 1, out, workspace, stream_, nullptr, 0,
+                              0, &pts)
+                 : solve_impl(nullptr, B, N, M, sentinel, has_pos_inf, 0, out, workspace,
+                              stream_, nullptr, 0, 0, &pts);
+}
+
+int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, int N, int M,
+                                    int D, int64_t *out, void *workspace,
+                                    size_t workspace_bytes, tm_stream_t stream_) {
+    cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+    if (B < 0 || N < 0 || M < 0 || D < 0) return TM_ERR_ARG;
+    if (B == 0 || N == 0 || M == 0)
+        return tm_jv_points_solve_f32(x, y, B, N, M, D, 0.0f, 0, 0, out, workspace,
+                                      workspace_bytes, stream_);
+    const int K = N > M ? N : M;
+    tmjv::StreamDevice scope(stream);
+    if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
     // check mode: every all-finite problem is solved and the statistics of
     // the computed cells are gathered in the same pass
-    int rc = solve_impl(nullptr, B, N, M, 0.0f, 0, 1, out, workspace, stream_, nullptr, 0, 0,
-                        &pts);
+    int rc = tm_jv_points_solve_f32(x, y, B, N, M, D, 0.0f, 0, 1, out, workspace,
+                                    workspace_bytes, stream_);
     if (rc) return rc;
     tm_jv_stats h{};
     const tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
@@ -1867,8 +1885,8 @@ int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, i
     if (rc) return rc;
     // +inf cells (coordinates at +-inf) need the batch-global sentinel
     if (pinf)
-        return solve_impl(nullptr, B, N, M, sentinel, 1, 0, out, workspace, stream_, nullptr, 0, 0,
-                          &pts);
+        return tm_jv_points_solve_f32(x, y, B, N, M, D, sentinel, 1, 0, out, workspace,
+                                      workspace_bytes, stream_);
     return TM_OK;
 }
 

@@ -17,7 +17,8 @@ spread one batch over several GPUs:
   copied back into one output on the caller's device.
 
 Both produce exactly what ``torch.ops.assignment.jonker_dense_batch`` gives
-on the whole batch.
+on the whole batch.  ``solve_points_sharded`` is the one-process-per-GPU
+form of the fused squared-Euclidean op (point sets in, no cost tensor).
 """
 
 from __future__ import annotations
@@ -159,6 +160,55 @@ def solve_sharded(local: torch.Tensor, group=None) -> torch.Tensor:
         if rc != 0:
             raise RuntimeError("batched JV kernel launch failed: "
                                + lib.tm_status_string(rc).decode())
+    return out
+
+
+def solve_points_sharded(x_local: torch.Tensor, y_local: torch.Tensor, group=None) -> torch.Tensor:
+    """``solve_sharded`` for the fused squared-Euclidean op: this rank's
+    contiguous slices x (B_r, N, D) and y (B_r, M, D) of one global batch of
+    point sets.  The costs are built inside the solve kernel on every rank
+    (tm_jv_points_solve_f32); the statistics of the computed cells are merged
+    with one all-reduce, exactly as for a cost batch, so the result equals
+    ``torch.ops.assignment.jonker_sqeuclidean_batch`` on the whole batch.
+    Collective over ``group``."""
+    import torch.distributed as dist
+
+    if x_local.dim() != 3 or y_local.dim() != 3 or x_local.shape[0] != y_local.shape[0] \
+            or x_local.shape[2] != y_local.shape[2]:
+        raise RuntimeError("x must be (B, N, D) and y (B, M, D)")
+    x = x_local.to(torch.float32).contiguous()
+    y = y_local.to(torch.float32).contiguous()
+    b, n, d = x.shape
+    m = y.shape[1]
+    k = max(n, m)
+    lib = _loader.core()
+    if k > lib.tm_jv_max_k():
+        raise RuntimeError(f"Batched JV (CUDA) supports max(N, M) <= 256, got K={k}")
+    nbytes = lib.tm_jv_points_workspace_bytes(b, n, m)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=x.device)
+    out = torch.full((b, n), -1, dtype=torch.long, device=x.device)
+    stream = _stream(x.device)
+
+    def launch(sentinel: float, pinf: int, check: int) -> None:
+        rc = lib.tm_jv_points_solve_f32(x.data_ptr(), y.data_ptr(), b, n, m, d, sentinel, pinf,
+                                        check, out.data_ptr(), ws.data_ptr(), nbytes, stream)
+        if rc != 0:
+            raise RuntimeError("batched JV kernel launch failed: "
+                               + lib.tm_status_string(rc).decode())
+
+    if b and n and m:
+        launch(0.0, 0, 1)
+    st = ws[:8].view(torch.int32)
+    if dist.get_backend(group) == "nccl":
+        t = _device_words(st)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+        words = t.cpu().tolist()
+    else:
+        flags, key = (int(v) & 0xFFFFFFFF for v in st.cpu().tolist())
+        words = merge_words(stats_words(flags, key), group)
+    sentinel, pinf = sentinel_from_words(words, k)
+    if pinf and b and n and m:
+        launch(sentinel, 1, 0)
     return out
 
 
