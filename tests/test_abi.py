@@ -91,3 +91,21 @@ def test_solve_argument_checks_need_no_gpu():
                                ctypes.c_void_p(64), None) == 5
     assert lib.tm_jv_workspace_bytes() == 64
     assert lib.tm_jonker_dense_batch_f32(None, 2, 3, 3, None, None, None) == 3
+
+
+def test_points_workspace_sizing_needs_no_gpu():
+    # TILE shapes need only the 256-byte header; streaming shapes take one
+    # N*M slab (rounded to 64 floats) per resident warp, at most one per problem
+    from torchmatch_b200 import _loader
+
+    lib = _loader.core()
+    assert lib.tm_jv_points_workspace_bytes(4096, 64, 64) == 256
+    assert lib.tm_jv_points_workspace_bytes(64, 130, 97) == 256
+    assert lib.tm_jv_points_workspace_bytes(1, 1, 256) == 256
+    assert lib.tm_jv_points_workspace_bytes(10, 256, 256) == 256 + 10 * 65536 * 4
+    slab = (200 * 150 + 63) // 64 * 64 * 4
+    assert lib.tm_jv_points_workspace_bytes(64, 200, 150) == 256 + 64 * slab
+    big = lib.tm_jv_points_workspace_bytes(65536, 256, 256) - 256
+    assert big % (65536 * 4) == 0 and 0 < big // (65536 * 4) <= 148 * 16
+    assert lib.tm_jv_points_workspace_bytes(0, 8, 8) == 256
+    assert lib.tm_jv_points_workspace_bytes(4, 300, 8) == 256
