@@ -230,8 +230,45 @@ def run_reference(args):
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
                          "sample": f"first {b} problems of the workload per step"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_gpu_kernel": reference_gpu_kernel(args, spec),
     }
     print(json.dumps(line), flush=True)
+
+
+def reference_gpu_kernel(args, spec):
+    """The reference's own batched CUDA kernel (cuda/jonker_tiled.cuh, built
+    from its sources into oracle/_ref for sm_100a) on the same resident
+    workload, CUDA events around K launches.  Kernel only: the reference op
+    also runs a statistics scan and an +inf rewrite first.  Its kernel takes
+    square K <= 64 (configs 1 and 2); otherwise None."""
+    import oracle
+
+    try:
+        import torch
+    except ImportError:
+        return None
+    if spec["N"] != spec["M"] or spec["N"] > 64 or not torch.cuda.is_available() \
+            or not oracle.reference_cuda_available():
+        return None
+    dev = torch.device("cuda", 0)
+    b = spec["B"]
+    per_bytes = b * spec["N"] * spec["M"] * 4
+    nbuf = max(1, min(8, -(-2 * L2_BYTES // per_bytes) + 1))
+    bufs = [make_batch_device(args.config, b, k, dev).contiguous() for k in range(nbuf)]
+    for k in range(args.warmup):
+        oracle.reference_cuda_jonker_dense_batch(bufs[k % nbuf])
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for k in range(args.steps):
+        oracle.reference_cuda_jonker_dense_batch(bufs[k % nbuf])
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    return {"value": b / (ms / 1e3), "unit": UNIT, "ms_per_launch": ms,
+            "kernel": "match_batch::lap_batch_kernel (reference cuda/jonker_tiled.cuh, "
+                      "nvcc sm_100a)", "inputs": "resident in HBM, rotating copies > 2x L2"}
 
 
 def run_ours(args):

@@ -122,3 +122,35 @@ def sqeuclidean_costs(x, y) -> np.ndarray:
 def jonker_sqeuclidean_batch(x, y, threads: int = 0) -> np.ndarray:
     """Oracle of the fused op: the restated producer, then jonker_dense_batch."""
     return jonker_dense_batch(sqeuclidean_costs(x, y), threads)
+
+
+REF_CUDA_LIB = HERE / "_ref" / "libtmref_cuda.so"
+
+
+def reference_cuda_available() -> bool:
+    return REF_CUDA_LIB.exists()
+
+
+def reference_cuda_jonker_dense_batch(costs):
+    """The reference's own batched CUDA kernel (cuda/jonker_tiled.cuh, built
+    from its sources for sm_100a) on a contiguous finite (B, K, K) float32
+    CUDA tensor, K <= 64, on the current stream.  Kernel only: the reference
+    op first scans for NaN / +-inf and rewrites +inf (absent here)."""
+    import torch
+
+    key = f"{REF_CUDA_LIB}:tmref_cuda_jonker_dense_batch"
+    if key not in _fns:
+        lib = ctypes.CDLL(str(REF_CUDA_LIB))
+        fn = lib.tmref_cuda_jonker_dense_batch
+        fn.restype = ctypes.c_int
+        fn.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                       ctypes.c_void_p]
+        _fns[key] = fn
+    b, k, k2 = costs.shape
+    if k != k2 or costs.dtype != torch.float32 or not costs.is_contiguous():
+        raise ValueError("costs must be a contiguous float32 (B, K, K) CUDA tensor")
+    out = torch.empty(b, k, dtype=torch.int64, device=costs.device)
+    rc = _fns[key](costs.data_ptr(), b, k, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    if rc != 0:
+        raise RuntimeError(f"reference CUDA kernel failed with code {rc}")
+    return out
