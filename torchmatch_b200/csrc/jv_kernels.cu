@@ -16,6 +16,9 @@
 //                 prefetched into L2 while the current one is solved.
 //   TILE = false  for matrices that do not fit next to enough warps, rows
 //                 are streamed from L2/HBM with read-only vector loads.
+// With PTS (fused cost construction) the kernel builds each problem's
+// squared-Euclidean costs from two point sets itself -- into the tile, or
+// into a per-warp slab of the workspace that then stands in for the input.
 //
 // Algorithm: the reference's CPU solver, reproduced step for step so the
 // mapping is identical on every input, ties included
@@ -1275,6 +1278,9 @@ __global__ void __launch_bounds__((TILE || S > 4 || PTS) ? 512 : 256, (TILE || S
         if (lane == 0) t = atomicAdd(P.ticket, 1ull);
         return (int64_t)__shfl_sync(kFull, t, 0);
     };
+    // columns per lane in the cost producer: one above S = 6, where the
+    // solver itself takes nearly all of the 128 registers a thread may use
+    constexpr int kFillCols = S > 6 ? 1 : 2;
     int64_t b = claim();
     while (b < P.B) {
         const int64_t nb = claim();
@@ -1283,15 +1289,18 @@ __global__ void __launch_bounds__((TILE || S > 4 || PTS) ? 512 : 256, (TILE || S
         TMJV_T(t_load);
         if constexpr (PTS && TILE) {
             // fused costs, TILE shape: build the problem in the tile itself
-            fill_cells<(S > 6) ? 1 : 2>(w.tile, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D,
-                           P.N, P.M, P.D, lane, P.sanitize != 0, P.sentinel);
+            fill_cells<kFillCols>(w.tile, P.px + b * (int64_t)P.N * P.D,
+                                  P.py + b * (int64_t)P.M * P.D, P.N, P.M, P.D, lane,
+                                  P.sanitize != 0, P.sentinel);
             __syncwarp();
             src = w.tile;
         } else if constexpr (PTS) {
             // fused costs, streaming shape: build the problem in this warp's slab
-            float *slab = P.slab + ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * P.slab_floats;
-            fill_cells<(S > 6) ? 1 : 2>(slab, P.px + b * (int64_t)P.N * P.D, P.py + b * (int64_t)P.M * P.D, P.N,
-                        P.M, P.D, lane, P.sanitize != 0, P.sentinel);
+            float *slab =
+                P.slab + ((int64_t)blockIdx.x * (blockDim.x >> 5) + warp) * P.slab_floats;
+            fill_cells<kFillCols>(slab, P.px + b * (int64_t)P.N * P.D,
+                                  P.py + b * (int64_t)P.M * P.D, P.N, P.M, P.D, lane,
+                                  P.sanitize != 0, P.sentinel);
             __syncwarp();  // orders the lanes' slab stores before the row reads
             src = slab;
         } else if constexpr (TILE) {
