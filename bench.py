@@ -642,6 +642,49 @@ def run_fused(args):
     print(json.dumps(line), flush=True)
 
 
+def run_scatter(args):
+    """One process, every visible GPU: the batch starts on cuda:0 and
+    sharded.solve_multi_gpu peer-copies contiguous slices out over NVLink,
+    solves them on their GPUs and copies the mappings back into one output on
+    cuda:0, all inside the timed region (CUDA events on cuda:0's stream, which
+    waits for every GPU's work).  Strong scaling: the whole batch is fixed."""
+    import torch
+
+    import torchmatch_b200  # noqa: F401
+    from torchmatch_b200 import sharded
+
+    spec = CONFIGS[args.config]
+    b = args.batch or spec["B"]
+    dev0 = torch.device("cuda", 0)
+    torch.cuda.set_device(dev0)
+    x = make_batch_device(args.config, b, 0, dev0)
+    ngpu = torch.cuda.device_count()
+    for _ in range(max(3, args.warmup)):
+        sharded.solve_multi_gpu(x)
+    for d in range(ngpu):
+        torch.cuda.synchronize(d)
+    steps = max(3, min(args.steps, 10))
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        out = sharded.solve_multi_gpu(x)
+    t1.record()
+    for d in range(ngpu):
+        torch.cuda.synchronize(d)
+    ms = t0.elapsed_time(t1) / steps
+    assert int(out.min()) >= -1
+    print(json.dumps({
+        "metric": METRIC, "value": b / (ms / 1e3), "unit": UNIT, "n_gpus": ngpu,
+        "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": spec["desc"], "global_batch": b,
+                   "parallelism": f"single process, {ngpu} GPUs, input and output on cuda:0 "
+                                  "(peer copies inside the timed region)"},
+    }), flush=True)
+
+
 def run_once(args):
     """Two calls of the op on one resident batch, nothing timed: the case the
     committed ncu summaries under profiles/ were captured on."""
@@ -670,6 +713,8 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="override B (with --once / --fused)")
     ap.add_argument("--streams", type=int, default=3,
                     help="streams of the pipelined (async op) measurement")
+    ap.add_argument("--scatter", action="store_true",
+                    help="one process over every visible GPU, batch scattered from cuda:0")
     ap.add_argument("--fused", action="store_true",
                     help="fused squared-Euclidean cost construction on config-5 point sets")
     args = ap.parse_args()
@@ -677,6 +722,8 @@ def main():
         run_once(args)
     elif args.fused:
         run_fused(args)
+    elif args.scatter:
+        run_scatter(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
