@@ -212,6 +212,19 @@ def solve_points_sharded(x_local: torch.Tensor, y_local: torch.Tensor, group=Non
     return out
 
 
+_PEER_STREAMS: dict[int, torch.cuda.Stream] = {}
+
+
+def _peer_stream(dev: torch.device) -> torch.cuda.Stream:
+    """One long-lived stream per GPU for solve_multi_gpu.  The caching
+    allocator keeps freed blocks per stream, so a fresh stream per call would
+    allocate every slice anew (and free the cache, which synchronises the
+    device, once memory runs short)."""
+    if dev.index not in _PEER_STREAMS:
+        _PEER_STREAMS[dev.index] = torch.cuda.Stream(dev)
+    return _PEER_STREAMS[dev.index]
+
+
 def shard_bounds(b: int, parts: int) -> list[tuple[int, int]]:
     """Contiguous slices [g * ceil(B / G), ...) of a batch of B problems."""
     step = -(-b // parts) if parts else 0
@@ -251,7 +264,7 @@ def solve_multi_gpu(costs: torch.Tensor, devices: list[int] | None = None) -> to
         if dev == home:
             local = (lo, hi)  # solved last, after the peers are under way
             continue
-        s = torch.cuda.Stream(dev)
+        s = _peer_stream(dev)
         with torch.cuda.device(dev), torch.cuda.stream(s):
             s.wait_event(ready)
             part = c[lo:hi].to(dev, non_blocking=True)
