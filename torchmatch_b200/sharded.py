@@ -267,6 +267,7 @@ def solve_multi_gpu(costs: torch.Tensor, devices: list[int] | None = None) -> to
         s = _peer_stream(dev)
         with torch.cuda.device(dev), torch.cuda.stream(s):
             s.wait_event(ready)
+            c.record_stream(s)  # s reads c: keep its block until s is done
             part = c[lo:hi].to(dev, non_blocking=True)
             res = _solve_local(part, sentinel, pinf)
             ev = torch.cuda.Event()
@@ -278,4 +279,5 @@ def solve_multi_gpu(costs: torch.Tensor, devices: list[int] | None = None) -> to
     for ev, res, lo, hi in done:
         home_stream.wait_event(ev)
         out[lo:hi].copy_(res, non_blocking=True)
+        res.record_stream(home_stream)  # read by the home stream after s
     return out
