@@ -94,3 +94,13 @@ def test_shard_bounds():
     assert sharded.shard_bounds(10, 4) == [(0, 3), (3, 6), (6, 9), (9, 10)]
     assert sharded.shard_bounds(2, 4) == [(0, 1), (1, 2), (2, 2), (2, 2)]
     assert sharded.shard_bounds(65536, 8)[7] == (57344, 65536)
+
+
+def test_solve_points_sharded_rejects_bad_shapes():
+    # shape checks run before any device work
+    with pytest.raises(RuntimeError, match="x must be"):
+        sharded.solve_points_sharded(torch.zeros(2, 3, 4), torch.zeros(2, 3, 5))
+    with pytest.raises(RuntimeError, match="x must be"):
+        sharded.solve_points_sharded(torch.zeros(2, 3, 4), torch.zeros(3, 3, 4))
+    with pytest.raises(RuntimeError, match="x must be"):
+        sharded.solve_points_sharded(torch.zeros(3, 4), torch.zeros(3, 4))
