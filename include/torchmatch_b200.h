@@ -37,7 +37,11 @@
  * exceptions.  Every function returns a tm_status code; CUDA errors are
  * reported as TM_ERR_CUDA and the cudaError_t is kept for tm_last_cuda_error().
  * Problems that hit a loop bound are reported through TM_WS_UNSOLVED in the
- * workspace status (their rows are -1), not through the return code.  All
+ * workspace status (their rows are -1, like the reference's rc != 0 rows,
+ * cpu/ops.cpp:274-278), not through the return code.  A tile copy whose
+ * wait runs out (TM_WS_TIMEOUT) leaves its problems as rows of -1 too; the
+ * synchronous entry points read the status back in their one
+ * synchronisation and return TM_ERR_TIMEOUT for it.  All
  * work is enqueued on the given stream; only the whole-op entry points
  * (tm_jonker_*_f32 except the async one) synchronise it, to read the
  * NaN / -inf verdict as the reference does.
@@ -61,7 +65,9 @@ typedef enum tm_status {
     TM_ERR_ARG = 3,        /* bad shape / null pointer / unsupported size     */
     TM_ERR_CUDA = 4,       /* a CUDA call failed; see tm_last_cuda_error()    */
     TM_ERR_TOO_LARGE = 5,  /* max(N, M) above tm_jv_max_k()                    */
-    TM_ERR_UNSOLVED = 6    /* a problem hit a loop bound (see TM_WS_UNSOLVED)  */
+    TM_ERR_UNSOLVED = 6,   /* a problem hit a loop bound (see TM_WS_UNSOLVED)  */
+    TM_ERR_TIMEOUT = 7     /* a cost tile copy did not land within the wait
+                              limit (TM_WS_TIMEOUT); its rows are -1          */
 } tm_status;
 
 /* Batch statistics, device-resident.  Written by tm_jv_stats_f32. */
@@ -145,10 +151,15 @@ int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M,
  * Its scratch is a fixed 64-byte array in this library's device memory, one
  * per GPU, kept until the process exits, so the only size limit is the
  * solver's own max(N, M) <= tm_jv_max_k() (TM_ERR_TOO_LARGE beyond it).
- * The first call on a device looks up that array's device address; make it
- * before any stream capture.  All calls on one device share the array:
- * calls that overlap on the GPU (other streams, other host threads) race
- * and must be serialised by the caller.  Nothing is allocated or freed. */
+ * The first call on a device looks up that array's device address and
+ * keeps it for the life of the process (a cudaDeviceReset does not refresh
+ * it); make that first call before any stream capture.  Every call
+ * synchronises its stream, as tm_jonker_dense_batch_f32 does.  All calls on
+ * one device share the array: calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller.  Because
+ * the caller cannot read the shared status word, problems left as rows of
+ * -1 by a loop bound are reported as TM_ERR_UNSOLVED, and a timed-out tile
+ * copy as TM_ERR_TIMEOUT.  Nothing is allocated or freed. */
 int tm_jonker_dense_batch_f32_noalloc(const float *costs, int64_t B, int N, int M,
                                       int64_t *out, tm_stream_t stream);
 
@@ -234,6 +245,16 @@ int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, i
  * Process-wide; not for production use.  No counterpart in the reference
  * (its CPU solver maps rc != 0 to a row of -1, cpu/ops.cpp:274-278). */
 void tm_jv_debug_set_loop_bound(int bound);
+
+/* Test hook: polls of a cost tile copy's mbarrier before the wait counts as
+ * timed out (0: the first wait gives up at once; a negative value restores
+ * the production limit), so tests can drive the timeout path -- rows of -1,
+ * TM_WS_TIMEOUT in the status, TM_ERR_TIMEOUT from the synchronous entry
+ * points -- without a GPU fault.  The copy in flight is still waited for
+ * (with the production limit) before its tile is reused.  Process-wide; not
+ * for production use.  No counterpart in the reference, whose kernel loads
+ * its tile with plain loads (cuda/jonker_tiled.cuh:64-71). */
+void tm_jv_debug_set_wait_limit(int limit);
 
 /* The cudaError_t of the last TM_ERR_CUDA on this thread. */
 int tm_last_cuda_error(void);

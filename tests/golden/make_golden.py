@@ -4,7 +4,8 @@ Runs the reference's own ``torch.ops.assignment.jonker_dense_batch`` and
 ``jonker_compact_batch`` (CPU backend of tue-p8n/torchmatch, cpu/ops.cpp:176-289)
 on every recipe of cases.py and stores their int64 outputs (as int16, the
 compact ones under ``compact__<case>``) plus the input digests.
-Needs the reference source tree; run in a container that has it:
+Needs the reference source tree: ``REF`` names its ``sources`` directory,
+by default the checkout beside this repository's (``<parent>/reference``):
 
     REF=/path/to/torchmatch/sources TORCHMATCH_FORCE_JIT=1 \
         TORCH_EXTENSIONS_DIR=/tmp/tm_ext python tests/golden/make_golden.py
@@ -20,7 +21,7 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-sys.path.insert(0, os.environ.get("REF", "/root/reference/sources"))
+sys.path.insert(0, os.environ.get("REF", str(HERE.parents[2] / "reference" / "sources")))
 sys.path.insert(0, str(HERE))
 
 import torch  # noqa: E402

@@ -38,3 +38,56 @@ def test_loop_bound_marks_rows_unsolved(lib, make, oracle_mod):
     out, status = torch.ops.assignment.jonker_dense_batch_async(x.cuda())
     assert int(status.item()) == 0
     np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
+@pytest.fixture
+def wait_lib():
+    import torchmatch_b200  # noqa: F401
+    from torchmatch_b200 import _loader
+
+    core = _loader.core()
+    yield core
+    core.tm_jv_debug_set_wait_limit(-1)
+
+
+def test_tile_wait_timeout_is_reported(wait_lib, oracle_mod):
+    """A tile copy whose bounded wait runs out (the hook makes the first wait
+    give up at once) leaves every problem as a row of -1, sets TM_WS_TIMEOUT
+    (bit 8) in the async op's status and makes the synchronous op raise; the
+    copy itself still lands before the tile is reused, and resetting the
+    hook brings back exact results."""
+    lib = wait_lib
+    x = config2(300)  # 64 x 64 problems are staged in shared memory by TMA
+    ref = oracle_mod.jonker_dense_batch(x.numpy())
+    xd = x.cuda()
+    lib.tm_jv_debug_set_wait_limit(0)
+    out, status = torch.ops.assignment.jonker_dense_batch_async(xd)
+    assert int(status.item()) & 8
+    assert (out.cpu().numpy() == -1).all()  # every row written, none left unset
+    with pytest.raises(RuntimeError, match="timed out"):
+        torch.ops.assignment.jonker_dense_batch(xd)
+    # through the C ABI: TM_ERR_TIMEOUT and rows of -1 over a poisoned buffer
+    ws = torch.zeros(lib.tm_jv_workspace_bytes(), dtype=torch.uint8, device="cuda")
+    got = torch.full((300, 64), 7, dtype=torch.long, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = lib.tm_jonker_dense_batch_f32(xd.data_ptr(), 300, 64, 64, got.data_ptr(),
+                                       ws.data_ptr(), stream)
+    assert rc == 7, lib.tm_status_string(rc)
+    assert (got.cpu().numpy() == -1).all()
+    lib.tm_jv_debug_set_wait_limit(-1)
+    np.testing.assert_array_equal(torch.ops.assignment.jonker_dense_batch(xd).cpu().numpy(), ref)
+    out, status = torch.ops.assignment.jonker_dense_batch_async(xd)
+    assert int(status.item()) == 0
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
+def test_sync_op_keeps_unsolved_rows_without_raising(lib, oracle_mod):
+    """A loop bound is not an error of the synchronous op: its problems come
+    back as rows of -1, as the reference's CPU solver returns them for
+    rc != 0 (cpu/ops.cpp:274-278)."""
+    x = config2(128)
+    ref = oracle_mod.jonker_dense_batch(x.numpy())
+    lib.tm_jv_debug_set_loop_bound(3)
+    got = torch.ops.assignment.jonker_dense_batch(x.cuda()).cpu().numpy()
+    bad = (got != ref).any(axis=1)
+    assert bad.any() and (got[bad] == -1).all()

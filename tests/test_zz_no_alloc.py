@@ -44,6 +44,52 @@ def test_noalloc_matches_regular_entry_point_twice():
         np.testing.assert_array_equal(got.cpu().numpy(), ref.cpu().numpy())
 
 
+def test_noalloc_allocates_nothing():
+    """Around warm calls, neither the device's free memory nor the torch
+    caching allocator's counters move: the entry point allocates nothing."""
+    from torchmatch_b200 import _loader
+
+    lib = _loader.core()
+    stream = torch.cuda.current_stream().cuda_stream
+    x = torch.rand(512, 64, 64, generator=torch.Generator().manual_seed(5)).cuda()
+    out = torch.empty(512, 64, dtype=torch.long, device="cuda")
+    # the first call loads the module and looks up the scratch address
+    assert lib.tm_jonker_dense_batch_f32_noalloc(x.data_ptr(), 512, 64, 64, out.data_ptr(),
+                                                 stream) == 0
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    stats0 = torch.cuda.memory_stats()
+    for _ in range(3):
+        assert lib.tm_jonker_dense_batch_f32_noalloc(x.data_ptr(), 512, 64, 64,
+                                                     out.data_ptr(), stream) == 0
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    stats1 = torch.cuda.memory_stats()
+    assert free1 == free0
+    for key in ("allocation.all.allocated", "segment.all.allocated", "num_alloc_retries"):
+        assert stats1.get(key, 0) == stats0.get(key, 0), key
+
+
+def test_noalloc_reports_unsolved_rows():
+    """The caller cannot read the shared status word, so rows that the loop
+    bound left as -1 come back as TM_ERR_UNSOLVED (6)."""
+    from torchmatch_b200 import _loader
+
+    lib = _loader.core()
+    stream = torch.cuda.current_stream().cuda_stream
+    x = torch.rand(64, 64, 64, generator=torch.Generator().manual_seed(6)).cuda()
+    out = torch.empty(64, 64, dtype=torch.long, device="cuda")
+    lib.tm_jv_debug_set_loop_bound(3)
+    try:
+        rc = lib.tm_jonker_dense_batch_f32_noalloc(x.data_ptr(), 64, 64, 64, out.data_ptr(),
+                                                   stream)
+    finally:
+        lib.tm_jv_debug_set_loop_bound(0)
+    assert rc == 6, lib.tm_status_string(rc)
+    assert lib.tm_jonker_dense_batch_f32_noalloc(x.data_ptr(), 64, 64, 64, out.data_ptr(),
+                                                 stream) == 0
+
+
 def test_noalloc_rejects_oversize_and_nan():
     from torchmatch_b200 import _loader
 

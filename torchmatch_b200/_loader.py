@@ -135,6 +135,8 @@ def core() -> ctypes.CDLL:
     lib.tm_jv_points_solve_f32.restype = i32
     lib.tm_jv_debug_set_loop_bound.argtypes = [i32]
     lib.tm_jv_debug_set_loop_bound.restype = None
+    lib.tm_jv_debug_set_wait_limit.argtypes = [i32]
+    lib.tm_jv_debug_set_wait_limit.restype = None
     lib.tm_status_string.restype = ctypes.c_char_p
     lib.tm_status_string.argtypes = [i32]
     for name in ("tm_jv_stats_f32", "tm_jv_sentinel", "tm_jv_solve_f32",
@@ -162,5 +164,6 @@ EXPORTED = (
     "tm_jv_points_solve_f32",
     "tm_last_cuda_error",
     "tm_jv_debug_set_loop_bound",
+    "tm_jv_debug_set_wait_limit",
     "tm_status_string",
 )

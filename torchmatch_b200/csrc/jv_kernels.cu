@@ -50,7 +50,7 @@ constexpr uint32_t kWaitLimit = 1u << 26;  // bounded mbarrier wait
 // Optional per-phase cycle counters (build with -DTMJV_PHASE_CLOCKS; the
 // kernel then adds clock64() deltas into tmjv_phase_cycles[]).
 #ifdef TMJV_PHASE_CLOCKS
-__device__ unsigned long long tmjv_phase_cycles[16];
+__device__ unsigned long long tmjv_phase_cycles[24];
 #define TMJV_T(name) const long long name = clock64()
 #define TMJV_ACC(idx, t0)                                                            \
     do {                                                                             \
@@ -96,6 +96,7 @@ struct Params {
     int warp_bytes;      // shared-memory bytes per warp
     int tile_floats;     // floats reserved for the staged tile (TILE mode)
     int bulk_ok;         // tile base and size are 16-byte multiples
+    uint32_t wait_limit; // polls of a tile copy's mbarrier before it counts as timed out
 };
 
 // ------------------------------------------------------------- statistics
@@ -130,6 +131,64 @@ __device__ __forceinline__ unsigned warp_min_u(unsigned x) {
     return __reduce_min_sync(kFull, x);
 }
 __device__ __forceinline__ int warp_max_i(int x) { return __reduce_max_sync(kFull, x); }
+
+// Ordered forms for the augmenting row reduction's step.  The step is one
+// dependent chain through shared-memory loads and warp reductions, which go
+// through one in-order pipe; written as volatile asm they keep the order
+// given here, so every load on the chain is issued as soon as its address is
+// known and no reduction whose result is needed later sits in front of it.
+// They carry no memory clobber: around them, plain C++ accesses to the same
+// arrays are fenced by __syncwarp(), which is a compiler barrier.
+__device__ __forceinline__ unsigned warp_min_u_ord(unsigned x) {
+    unsigned r;
+    asm volatile("redux.sync.min.u32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(kFull));
+    return r;
+}
+__device__ __forceinline__ int lds_s16(const int16_t *p) {
+    int r;
+    asm volatile("ld.shared.s16 %0, [%1];" : "=r"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)));
+    return r;
+}
+__device__ __forceinline__ float lds_f32(const float *p) {
+    float r;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)));
+    return r;
+}
+__device__ __forceinline__ void sts_s16(int16_t *p, int x) {
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(p)),
+                 "h"((unsigned short)x)
+                 );
+}
+__device__ __forceinline__ void sts_s32(int32_t *p, int x) {
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(p)), "r"(x)
+                 );
+}
+__device__ __forceinline__ void sts_f32(float *p, float x) {
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"((uint32_t)__cvta_generic_to_shared(p)), "f"(x)
+                 );
+}
+// Row i of a square tile whose K is a multiple of 32 * VEC (no padding),
+// VEC consecutive columns per lane and group, in issue order.
+template <int S, int VEC>
+__device__ __forceinline__ void lds_row_full(const float *tile, int i, int lane, float (&c)[S]) {
+    const uint32_t base =
+        (uint32_t)__cvta_generic_to_shared(tile + i * (32 * S) + lane * VEC);
+#pragma unroll
+    for (int g = 0; g < S / VEC; ++g) {
+        const uint32_t a = base + g * 32 * VEC * 4;
+        if constexpr (VEC == 4) {
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(c[g * 4]), "=f"(c[g * 4 + 1]), "=f"(c[g * 4 + 2]), "=f"(c[g * 4 + 3])
+                         : "r"(a));
+        } else if constexpr (VEC == 2) {
+            asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];"
+                         : "=f"(c[g * 2]), "=f"(c[g * 2 + 1])
+                         : "r"(a));
+        } else {
+            asm volatile("ld.shared.f32 %0, [%1];" : "=f"(c[g]) : "r"(a));
+        }
+    }
+}
 
 template <int S, int VEC>
 struct Layout {
@@ -524,6 +583,220 @@ __device__ void emit_result(const Params &P, WarpShared &w, int lane, int64_t b,
     __syncwarp();
 }
 
+// ------------------------------------------- augmenting row reduction
+// The two passes of the augmenting row reduction (jonker_dense_flat.h:178-235,
+// called twice at :265-269) for rows read directly (shared-memory tile, or
+// streamed rows without the row cache).  Step semantics are those of the
+// reference's scalar loop; the layout only shortens the dependent chain of
+// one step, which bounds the phase:
+//   * the prices v stay in the lanes' registers for the row scans and are
+//     mirrored in shared memory (the event buffer of the Dijkstra phase is
+//     free during this phase), as is the row of each column (ycol), so the
+//     owner lookups of the chosen column are single broadcast loads;
+//   * the second minimum waits for the first index instead of a tie ballot:
+//     the lane holding column j1 offers its own second value, every other
+//     lane its best one, so a second lane at v1 makes v2 = v1;
+//   * the successor row of a lowering step (the previous owner of j1) is
+//     loaded as soon as its index is known, ahead of the step's decisions,
+//     and in TILE mode the next queued row is loaded ahead as well, so the
+//     next step starts from registers whichever way the step decides;
+//   * shared-memory accesses and reductions are volatile asm issued in the
+//     order written, so no load on the chain waits behind a later one;
+//   * a step commits through selects, not branches: the common step has no
+//     branch but the loop's own.  The two rare cases -- a second value at or
+//     above the initial LARGE, and a tie that switches the row to j2 --
+//     leave the step uncommitted and end the fast loop; that step is then
+//     run by the general code below it.
+// Returns true when a pass hit its loop bound.
+template <int S, int VEC, bool TILE, bool FULL, bool PTS>
+__device__ __forceinline__ bool arr_direct(const float *__restrict__ src, const Params &P,
+                                           WarpShared &w, int lane, int N, int M, int K,
+                                           bool sanitize, float sentinel, const int (&jj)[S],
+                                           unsigned valid, float (&v)[S], int &nfree) {
+    // rows of a padding-free tile come through the ordered loads
+    auto row_of = [&](int i, float (&c)[S]) {
+        if constexpr (TILE && FULL) lds_row_full<S, VEC>(src, i, lane, c);
+        else load_row<S, VEC, TILE, FULL, PTS>(src, i, N, M, lane, sanitize, sentinel, c);
+    };
+    // K a power of two: the speculative successor of a step whose column was
+    // free (i0 = -1) is read from row K - 1 by a mask instead of a select
+    constexpr bool kMask = TILE && FULL && (S & (S - 1)) == 0;
+    float *vsh = reinterpret_cast<float *>(w.evbuf);
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+        if (valid >> s & 1) vsh[jj[s]] = v[s];
+    __syncwarp();
+    const bool compact = P.compact != 0;
+    const float big2 = compact ? FLT_MAX : kBig;
+    const float inf = __int_as_float(0x7f800000);
+    bool failed = false;
+    for (int pass = 0; pass < 2 && nfree > 0 && !failed; ++pass) {
+        unsigned head = 0, visits = 0;
+        int kept = 0;
+        unsigned cap = compact ? 64u * (unsigned)K * (unsigned)K + 4096u
+                               : (unsigned)K * (unsigned)K + 2u * K + 8u;
+        if (P.loop_bound && (unsigned)P.loop_bound < cap) cap = (unsigned)P.loop_bound;
+        const unsigned nf = (unsigned)nfree;
+        int row = w.queue[0];
+        // the queued row of the coming step (push-backs only write consumed
+        // slots, so this slot is stable until it is consumed)
+        int qnext = w.queue[1 < nf ? 1 : 0];
+        float c[S];
+        row_of(row, c);
+        __syncwarp();
+        while (head < nf && visits < cap) {
+            bool rare = false;
+            // ---- fast steps
+            do {
+                const unsigned h1 = head + 1, vis1 = visits + 1;
+                const int queued = qnext;
+                // lane-local lexicographic (value, column) top-2; the slots
+                // of a lane ascend in column
+                float a1 = c[0] - v[0], a2 = inf;
+                int c1 = jj[0], c2 = 0x7fffffff;
+#pragma unroll
+                for (int t = 1; t < S; ++t) {
+                    const float x = c[t] - v[t];
+                    if (x < a1) { a2 = a1; c2 = c1; a1 = x; c1 = jj[t]; }
+                    else if (x < a2) { a2 = x; c2 = jj[t]; }
+                }
+                (void)c2;
+                const float v1 = warp_min_f(a1);
+                const int j1 = (int)warp_min_u_ord(a1 == v1 ? (unsigned)c1 : 0xffffffffu);
+                const int i0 = lds_s16(w.ycol + j1);
+                const float vj1 = lds_f32(vsh + j1);
+                const float v2 = warp_min_f(c1 == j1 ? a2 : a1);
+                float cn[S], cq[S];
+                if constexpr (kMask) row_of(i0 & (K - 1), cn);
+                else row_of(i0 >= 0 ? i0 : row, cn);
+                if constexpr (TILE) row_of(queued, cq);
+                // rr_cnt < current * n (absent from the compact variant)
+                const bool early = compact || vis1 < h1 * (unsigned)K;
+                const float lowered = vj1 - (v2 - v1);
+                const bool lowers = lowered < vj1;
+                rare = !(v2 < big2) || (early && !lowers && i0 >= 0);
+                const bool lower_now = early && lowers && !rare;
+                const bool push_front = i0 >= 0 && lower_now;
+                const bool push_back = i0 >= 0 && !push_front && !rare;
+                // every lane stores the same words; a rare step stores
+                // the old values back (ycol, vsh), a slot that is free
+                // (queue) or a word the rare step rewrites (xrow)
+                sts_f32(vsh + j1, lower_now ? lowered : vj1);
+#pragma unroll
+                for (int t = 0; t < S; ++t) v[t] = (lower_now && jj[t] == j1) ? lowered : v[t];
+                sts_s16(w.ycol + j1, rare ? i0 : row);
+                sts_s32(w.xrow + row, j1);
+                sts_s16(w.queue + kept, i0);
+                kept += push_back;
+                head = rare ? head : h1 - push_front;
+                visits = rare ? visits : vis1;
+                const int nrow = push_front ? i0 : queued;
+                qnext = lds_s16(w.queue + (head + 1 < nf ? head + 1 : 0));
+                if constexpr (TILE) {
+#pragma unroll
+                    for (int t = 0; t < S; ++t) c[t] = rare ? c[t] : (push_front ? cn[t] : cq[t]);
+                    row = rare ? row : nrow;
+                } else {
+                    if (!rare) {
+                        row = nrow;
+                        if (push_front) {
+#pragma unroll
+                            for (int t = 0; t < S; ++t) c[t] = cn[t];
+                        } else {
+                            row_of(row, c);
+                        }
+                    }
+                }
+            } while (!rare && head < nf && visits < cap);
+            if (!rare) break;
+            // ---- one general step on `row` (uncommitted by the fast loop)
+            __syncwarp();
+            ++visits;
+            ++head;
+            const int queued = w.queue[head < nf ? head : 0];
+            float a1 = c[0] - v[0], a2 = inf;
+            int c1 = jj[0], c2 = 0x7fffffff;
+#pragma unroll
+            for (int t = 1; t < S; ++t) {
+                const float x = c[t] - v[t];
+                if (x < a1) { a2 = a1; c2 = c1; a1 = x; c1 = jj[t]; }
+                else if (x < a2) { a2 = x; c2 = jj[t]; }
+            }
+            float v1 = warp_min_f(a1);
+            int j1 = (int)warp_min_u(a1 == v1 ? (unsigned)c1 : 0xffffffffu);
+            const bool mine = c1 == j1;
+            const float bv = mine ? a2 : a1;
+            const int bc = mine ? c2 : c1;
+            float v2 = warp_min_f(bv);
+            int j2 = -2;  // -2: not computed yet
+            if (!(v2 < big2)) {
+                // a reduced cost at or above LARGE: replay the scalar scan
+                // of :193-210 exactly (not the plain top-2 then)
+#pragma unroll
+                for (int t = 0; t < S; ++t)
+                    if (valid >> t & 1) w.dist[jj[t]] = c[t] - v[t];
+                __syncwarp();
+                int ja = 0, jb = -1;
+                float va = 0.0f, vb = big2;
+                if (lane == 0) {
+                    va = w.dist[0];
+                    for (int j = 1; j < K; ++j) {
+                        const float t = w.dist[j];
+                        if (t < vb) {
+                            if (t >= va) { vb = t; jb = j; }
+                            else { vb = va; jb = ja; va = t; ja = j; }
+                        }
+                    }
+                }
+                j1 = __shfl_sync(kFull, ja, 0);
+                j2 = __shfl_sync(kFull, jb, 0);
+                v1 = __shfl_sync(kFull, va, 0);
+                v2 = __shfl_sync(kFull, vb, 0);
+                __syncwarp();
+            }
+            int i0 = w.ycol[j1];
+            const float vj1 = vsh[j1];
+            const bool early = compact || visits < head * (unsigned)K;
+            const float lowered = vj1 - (v2 - v1);
+            const bool lowers = lowered < vj1;
+            int jsel = j1;
+            if (early && !lowers && i0 >= 0) {
+                if (j2 == -2) j2 = (int)warp_min_u(bv == v2 ? (unsigned)bc : 0xffffffffu);
+                if (j2 >= 0) {
+                    jsel = j2;
+                    i0 = w.ycol[j2];
+                }
+            }
+            const bool lower_now = early && lowers;
+            const bool push_front = i0 >= 0 && lower_now;
+            const bool push_back = i0 >= 0 && !push_front;
+            __syncwarp();
+            if (lower_now) {
+                vsh[j1] = lowered;
+#pragma unroll
+                for (int t = 0; t < S; ++t) v[t] = jj[t] == j1 ? lowered : v[t];
+            }
+            w.ycol[jsel] = (int16_t)row;
+            w.xrow[row] = jsel;
+            if (push_back) w.queue[kept] = (int16_t)i0;
+            kept += push_back;
+            head -= push_front;
+            row = push_front ? i0 : queued;
+            __syncwarp();
+            qnext = w.queue[head + 1 < nf ? head + 1 : 0];
+            row_of(row, c);
+            __syncwarp();
+        }
+#ifdef TMJV_PHASE_CLOCKS
+        if (lane == 0) atomicAdd(&tmjv_phase_cycles[5], (unsigned long long)visits);
+#endif
+        if (head < nf) failed = true;  // loop bound reached
+        nfree = kept;
+        __syncwarp();
+    }
+    return failed;
+}
+
 // ------------------------------------------------------------- one solve
 template <int S, int VEC, bool TILE, bool FULL, bool PTS>
 __device__ void solve_problem(const float *__restrict__ src, const Params &P, WarpShared &w,
@@ -703,6 +976,13 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     // broadcast loads, updates single stores); the lane registers are
     // refreshed on misses and at the end of the phase.
     constexpr bool use_cache = kCached && S >= 7;
+    // TILE rows: the ordered, branch-free step (arr_direct).  Streamed rows
+    // keep the loop below, whose step waits on a global load anyway (the
+    // ordered step measured slower there).
+    if constexpr (TILE) {
+        failed = arr_direct<S, VEC, TILE, FULL, PTS>(src, P, w, lane, N, M, K, sanitize,
+                                                     sentinel, jj, valid, v, nfree);
+    } else {
     if (use_cache) {
 #pragma unroll
         for (int s = 0; s < S; ++s) {
@@ -927,15 +1207,13 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     if constexpr (use_cache) {
 #pragma unroll
         for (int s = 0; s < S; ++s)
-            if (valid >> s & 1) {
-                v[s] = w.vsh[jj[s]];
-                yc[s] = w.ycol[jj[s]];
-            }
+            if (valid >> s & 1) v[s] = w.vsh[jj[s]];
     } else {
 #pragma unroll
         for (int s = 0; s < S; ++s)
             if (valid >> s & 1) w.ycol[jj[s]] = (int16_t)yc[s];
     }
+    }  // streamed rows
     __syncwarp();
 
     TMJV_ACC(3, t_arr);
@@ -1218,8 +1496,8 @@ __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t b
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
-__device__ __forceinline__ bool bar_wait(uint64_t *bar, uint32_t phase) {
-    for (uint32_t it = 0; it < kWaitLimit; ++it) {
+__device__ __forceinline__ bool bar_wait(uint64_t *bar, uint32_t phase, uint32_t limit) {
+    for (uint32_t it = 0; it < limit; ++it) {
         uint32_t done;
         asm volatile(
             "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
@@ -1307,14 +1585,29 @@ __global__ void __launch_bounds__((TILE || S > 4 || PTS) ? 512 : 256, (TILE || S
             bool ok = true;
             if (P.bulk_ok) {
                 if (lane == 0) bulk_load(w.tile, g, tile_bytes, w.bar);
-                ok = bar_wait(w.bar, phase);
+                ok = bar_wait(w.bar, phase, P.wait_limit);
+                if (!__all_sync(kFull, ok)) {
+                    // The copy did not land in time: report it and leave the
+                    // problem as a row of -1 rather than unwritten.  The copy
+                    // in flight gets a second bounded wait before the tile
+                    // may be reused; if it never lands, this warp issues no
+                    // further copies and writes every problem it still
+                    // claims as a row of -1.
+                    if (lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_WS_TIMEOUT);
+                    const bool landed = __all_sync(kFull, bar_wait(w.bar, phase, kWaitLimit));
+                    phase ^= 1u;
+                    emit_result(P, w, lane, b, P.N, P.M, false);
+                    if (!landed) {
+                        for (int64_t q = nb; q < P.B; q = claim())
+                            emit_result(P, w, lane, q, P.N, P.M, false);
+                        return;
+                    }
+                    b = nb;
+                    continue;
+                }
                 phase ^= 1u;
             } else {
                 for (int64_t k = lane; k < per; k += 32) w.tile[k] = __ldg(g + k);
-            }
-            if (!__all_sync(kFull, ok)) {
-                if (lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_WS_TIMEOUT);
-                return;
             }
             if (P.sanitize) {
                 for (int64_t k = lane; k < per; k += 32)
@@ -1364,6 +1657,9 @@ __global__ void __launch_bounds__(256) jv_stats_kernel(const float *__restrict__
 static thread_local int g_last_cuda = 0;
 // test hook (tm_jv_debug_set_loop_bound): caps every solver loop
 static int g_loop_bound = 0;
+// test hook (tm_jv_debug_set_wait_limit): polls of a tile copy's mbarrier
+// before the wait counts as timed out (-1: the production limit)
+static long long g_wait_limit = -1;
 
 static int cuda_fail(cudaError_t e) {
     g_last_cuda = (int)e;
@@ -1607,6 +1903,8 @@ int tm_jv_max_k(void) { return 32 * tmjv::kMaxSlots; }
 
 void tm_jv_debug_set_loop_bound(int bound) { tmjv::g_loop_bound = bound > 0 ? bound : 0; }
 
+void tm_jv_debug_set_wait_limit(int limit) { tmjv::g_wait_limit = limit < 0 ? -1 : limit; }
+
 int tm_last_cuda_error(void) { return tmjv::g_last_cuda; }
 
 const char *tm_status_string(int status) {
@@ -1619,6 +1917,8 @@ const char *tm_status_string(int status) {
     case TM_ERR_CUDA: return "batched JV kernel launch failed (CUDA error)";
     case TM_ERR_TOO_LARGE: return "batched JV (CUDA) supports max(N, M) <= 256";
     case TM_ERR_UNSOLVED: return "a problem exceeded the solver's loop bound";
+    case TM_ERR_TIMEOUT:
+        return "batched JV kernel: a wait for a cost tile copy timed out (rows of -1 written)";
     default: return "unknown status";
     }
 }
@@ -1703,6 +2003,7 @@ static int solve_impl(const float *costs, int64_t B, int N, int M, float sentine
     P.gated = gated;
     P.l2_prefetch = tmjv::l2_prefetch_enabled();
     P.loop_bound = tmjv::g_loop_bound;
+    P.wait_limit = tmjv::g_wait_limit < 0 ? tmjv::kWaitLimit : (uint32_t)tmjv::g_wait_limit;
     P.stats = &ws->stats;
     P.out = out;
     if (u) {
@@ -1737,8 +2038,32 @@ int tm_jv_solve_checked_f32(const float *costs, int64_t B, int N, int M, int64_t
 
 size_t tm_jv_workspace_bytes(void) { return sizeof(tm_jv_workspace); }
 
+// Copies the workspace header (statistics and status) back to the host in
+// one transfer and waits for the stream: the single synchronisation of the
+// synchronous entry points.
+static int read_workspace(void *workspace, cudaStream_t stream, tm_jv_workspace *h) {
+    cudaError_t e = cudaMemcpyAsync(h, workspace, sizeof(*h), cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    return TM_OK;
+}
+
+// Return code of a finished synchronous call from its device status.  A tile
+// copy that timed out is an error (its rows were written as -1).  Rows that a
+// loop bound left as -1 are not: the reference's CPU solver maps a failed
+// problem to a row of -1 the same way (cpu/ops.cpp:274-278); the status word
+// still carries TM_WS_UNSOLVED for callers that read it.
+static int status_code(int32_t status) {
+    return (status & TM_WS_TIMEOUT) ? TM_ERR_TIMEOUT : TM_OK;
+}
+
+// Check-mode solve, one read-back of the verdict, and a sentinel re-solve
+// only for a batch holding +inf (then read back again for its status).
+// `status_out` (may be null) receives the final TM_WS_* bits.
 static int full_op(const float *costs, int64_t B, int N, int M, int64_t *out,
-                   void *workspace, tm_stream_t stream_, int compact) {
+                   void *workspace, tm_stream_t stream_, int compact,
+                   int32_t *status_out = nullptr) {
     cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
     if (B < 0 || N < 0 || M < 0) return TM_ERR_ARG;
     if (B == 0 || N == 0) return TM_OK;
@@ -1751,21 +2076,23 @@ static int full_op(const float *costs, int64_t B, int N, int M, int64_t *out,
     // one pass solves every all-finite problem and gathers the statistics
     int rc = solve_impl(costs, B, N, M, 0.0f, 0, 1, out, workspace, stream_, nullptr, 0, compact);
     if (rc) return rc;
-    tm_jv_stats h{};
-    const tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
-    cudaError_t e = cudaMemcpyAsync(&h, st, sizeof(h), cudaMemcpyDeviceToHost, stream);
-    if (e != cudaSuccess) return tmjv::cuda_fail(e);
-    e = cudaStreamSynchronize(stream);
-    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    tm_jv_workspace h{};
+    rc = read_workspace(workspace, stream, &h);
+    if (rc) return rc;
     float sentinel = 1.0f;
     int pinf = 0;
-    rc = tm_jv_sentinel(&h, K, &sentinel, &pinf);
+    rc = tm_jv_sentinel(&h.stats, K, &sentinel, &pinf);
     if (rc) return rc;
     // +inf cells need the batch-global sentinel: solve again with it
-    if (pinf)
-        return solve_impl(costs, B, N, M, sentinel, 1, 0, out, workspace, stream_, nullptr, 0,
-                          compact);
-    return TM_OK;
+    if (pinf) {
+        rc = solve_impl(costs, B, N, M, sentinel, 1, 0, out, workspace, stream_, nullptr, 0,
+                        compact);
+        if (rc) return rc;
+        rc = read_workspace(workspace, stream, &h);
+        if (rc) return rc;
+    }
+    if (status_out) *status_out = h.status;
+    return status_code(h.status);
 }
 
 int tm_jonker_dense_batch_f32(const float *costs, int64_t B, int N, int M, int64_t *out,
@@ -1803,20 +2130,21 @@ static int full_unpacked(const float *costs, int64_t B, int N, int M,
     if (scope.err != cudaSuccess) return tmjv::cuda_fail(scope.err);
     int rc = solve_impl(costs, B, N, M, 0.0f, 0, 1, nullptr, workspace, stream_, u, 0, compact);
     if (rc) return rc;
-    tm_jv_stats h{};
-    const tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
-    cudaError_t e = cudaMemcpyAsync(&h, st, sizeof(h), cudaMemcpyDeviceToHost, stream);
-    if (e != cudaSuccess) return tmjv::cuda_fail(e);
-    e = cudaStreamSynchronize(stream);
-    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    tm_jv_workspace h{};
+    rc = read_workspace(workspace, stream, &h);
+    if (rc) return rc;
     float sentinel = 1.0f;
     int pinf = 0;
-    rc = tm_jv_sentinel(&h, K, &sentinel, &pinf);
+    rc = tm_jv_sentinel(&h.stats, K, &sentinel, &pinf);
     if (rc) return rc;
-    if (pinf)
-        return solve_impl(costs, B, N, M, sentinel, 1, 0, nullptr, workspace, stream_, u, 0,
-                          compact);
-    return TM_OK;
+    if (pinf) {
+        rc = solve_impl(costs, B, N, M, sentinel, 1, 0, nullptr, workspace, stream_, u, 0,
+                        compact);
+        if (rc) return rc;
+        rc = read_workspace(workspace, stream, &h);
+        if (rc) return rc;
+    }
+    return status_code(h.status);
 }
 
 int tm_jonker_dense_batch_unpacked_f32(const float *costs, int64_t B, int N, int M,
@@ -1882,21 +2210,22 @@ int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, i
     int rc = tm_jv_points_solve_f32(x, y, B, N, M, D, 0.0f, 0, 1, out, workspace,
                                     workspace_bytes, stream_);
     if (rc) return rc;
-    tm_jv_stats h{};
-    const tm_jv_stats *st = &reinterpret_cast<tm_jv_workspace *>(workspace)->stats;
-    cudaError_t e = cudaMemcpyAsync(&h, st, sizeof(h), cudaMemcpyDeviceToHost, stream);
-    if (e != cudaSuccess) return tmjv::cuda_fail(e);
-    e = cudaStreamSynchronize(stream);
-    if (e != cudaSuccess) return tmjv::cuda_fail(e);
+    tm_jv_workspace h{};
+    rc = read_workspace(workspace, stream, &h);
+    if (rc) return rc;
     float sentinel = 1.0f;
     int pinf = 0;
-    rc = tm_jv_sentinel(&h, K, &sentinel, &pinf);
+    rc = tm_jv_sentinel(&h.stats, K, &sentinel, &pinf);
     if (rc) return rc;
     // +inf cells (coordinates at +-inf) need the batch-global sentinel
-    if (pinf)
-        return tm_jv_points_solve_f32(x, y, B, N, M, D, sentinel, 1, 0, out, workspace,
-                                      workspace_bytes, stream_);
-    return TM_OK;
+    if (pinf) {
+        rc = tm_jv_points_solve_f32(x, y, B, N, M, D, sentinel, 1, 0, out, workspace,
+                                    workspace_bytes, stream_);
+        if (rc) return rc;
+        rc = read_workspace(workspace, stream, &h);
+        if (rc) return rc;
+    }
+    return status_code(h.status);
 }
 
 }  // extern "C"
@@ -1905,8 +2234,8 @@ int tm_jonker_sqeuclidean_batch_f32(const float *x, const float *y, int64_t B, i
 // Reads and clears the per-phase cycle counters (debug builds only).
 extern "C" int tm_phase_read(unsigned long long *host8) {
     cudaDeviceSynchronize();
-    cudaMemcpyFromSymbol(host8, tmjv::tmjv_phase_cycles, sizeof(unsigned long long) * 16);
-    unsigned long long z[16] = {0};
+    cudaMemcpyFromSymbol(host8, tmjv::tmjv_phase_cycles, sizeof(unsigned long long) * 24);
+    unsigned long long z[24] = {0};
     cudaMemcpyToSymbol(tmjv::tmjv_phase_cycles, z, sizeof(z));
     return 0;
 }
@@ -1947,6 +2276,11 @@ extern "C" int tm_jonker_dense_batch_f32_noalloc(const float *costs, int64_t B, 
         }
         ws = g_noalloc_ptr[scope.dev];
     }
-    // the regular entry point zeroes the statistics and the work ticket
-    return tm_jonker_dense_batch_f32(costs, B, N, M, out, ws, stream_);
+    // the regular op body zeroes the statistics, ticket and status, and
+    // hands back the final status word: this caller has no other way to
+    // read it, so rows left -1 by a loop bound come back as TM_ERR_UNSOLVED
+    int32_t status = 0;
+    const int rc = full_op(costs, B, N, M, out, ws, stream_, 0, &status);
+    if (rc) return rc;
+    return (status & TM_WS_UNSOLVED) ? TM_ERR_UNSOLVED : TM_OK;
 }

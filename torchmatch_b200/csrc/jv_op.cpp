@@ -10,7 +10,8 @@
 // Behaviour kept from jonker_dense_batch_cuda (cuda/dispatch.cu:137-177):
 // device guard, current-stream execution, refusal inside CUDA graph capture,
 // fp32 cast, batch-global +inf sentinel with a host sync to raise on NaN /
-// -inf, a fresh int64 (B, N) output.  The statistics come out of the solve
+// -inf, a fresh int64 (B, N) output.  The same sync reads the device status
+// back and raises if a cost tile copy timed out.  The statistics come out of the solve
 // itself (check mode); only batches holding +inf are solved a second time.  Widened: rectangular (B, N, M) input
 // and max(N, M) up to tm_jv_max_k(); non-contiguous input is made
 // contiguous instead of rejected.  All device work goes through the C ABI in
@@ -79,6 +80,7 @@ at::Tensor packed_op(const at::Tensor &costs, FullFn fn, const char *name) {
                       reinterpret_cast<tm_stream_t>(stream));
     TORCH_CHECK(rc != TM_ERR_NAN, name, ": ", tm_status_string(rc));
     TORCH_CHECK(rc != TM_ERR_NEG_INF, name, ": ", tm_status_string(rc));
+    TORCH_CHECK(rc != TM_ERR_TIMEOUT, name, ": ", tm_status_string(rc));
     TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
     return out;
 }
@@ -124,6 +126,7 @@ unpacked_op(const at::Tensor &costs, UnpackedFn fn, const char *name) {
         scratch.mutable_data_ptr(), reinterpret_cast<tm_stream_t>(stream));
     TORCH_CHECK(rc != TM_ERR_NAN, name, ": ", tm_status_string(rc));
     TORCH_CHECK(rc != TM_ERR_NEG_INF, name, ": ", tm_status_string(rc));
+    TORCH_CHECK(rc != TM_ERR_TIMEOUT, name, ": ", tm_status_string(rc));
     TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
     return {matches, ur, uc, nm};
 }
@@ -213,6 +216,7 @@ at::Tensor jonker_sqeuclidean_batch_cuda(const at::Tensor &x, const at::Tensor &
         scratch.mutable_data_ptr(), ws_bytes, reinterpret_cast<tm_stream_t>(stream));
     TORCH_CHECK(rc != TM_ERR_NAN, "jonker_sqeuclidean_batch: ", tm_status_string(rc));
     TORCH_CHECK(rc != TM_ERR_NEG_INF, "jonker_sqeuclidean_batch: ", tm_status_string(rc));
+    TORCH_CHECK(rc != TM_ERR_TIMEOUT, "jonker_sqeuclidean_batch: ", tm_status_string(rc));
     TORCH_CHECK(rc == TM_OK, "batched JV kernel launch failed: ", status_text(rc));
     return out;
 }
