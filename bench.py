@@ -26,11 +26,18 @@ each timed step.  `roofline` is measured live: the solve kernel alone,
 launched through the C ABI between CUDA events on its stream, against the
 measured HBM copy bandwidth.  `cpu_baseline` times the reference's own CPU
 solver (oracle/_ref, built from the reference sources) on the host cores.
+
+Every named shape is reported in the same line: `per_config` (one GPU) gives,
+for c1, c3, c4 and c5, the op's problems/s on the whole named batch, its solve
+launch's roofline fraction and the reference CPU solver on this host, and
+`strong_c5` (every N) gives config 5 as strong scaling -- the fixed
+B = 65536 batch split over the N ranks, max over ranks.
 """
 
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -271,6 +278,117 @@ def reference_gpu_kernel(args, spec):
                       "nvcc sm_100a)", "inputs": "resident in HBM, rotating copies > 2x L2"}
 
 
+def _device_ms(fn, steps: int, warmup: int) -> float:
+    """Mean ms per call of fn() between CUDA events on the current stream."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        fn()
+    t1.record()
+    torch.cuda.synchronize()
+    return t0.elapsed_time(t1) / steps
+
+
+def per_config_record(cfg: str, dev, lib, args, peak: float) -> dict:
+    """One GPU, the whole named batch of `cfg` resident in HBM: the op
+    (device-timed per call), its dominant solve launch alone through the C
+    ABI (the roofline kernel), and the reference's CPU solver on a bounded
+    sample on this host.  Inputs: one batch larger than 2x L2 for c3-c5;
+    c1 is a 256 KB launch-bound case that stays in L2."""
+    import torch
+
+    spec = CONFIGS[cfg]
+    b, n, m = spec["B"], spec["N"], spec["M"]
+    x = make_batch_device(cfg, b, 11, dev).contiguous()
+    op = torch.ops.assignment.jonker_dense_batch
+    steps = {"c1": 50, "c3": 20, "c4": 20, "c5": 3}.get(cfg, 20)
+    op_ms = _device_ms(lambda: op(x), steps, 2)
+    ws = torch.zeros(lib.tm_jv_workspace_bytes() // 4, dtype=torch.int32, device=dev)
+    out = torch.empty(b, n, dtype=torch.long, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    has_inf = bool(torch.isinf(x).any())
+    if has_inf:
+        # the op's second launch, with the batch-global sentinel, is the one
+        # that solves every problem; time that launch
+        fin = x[torch.isfinite(x)]
+        sent = (float(fin.max()) + 1.0) * float(max(n, m) + 1) if fin.numel() else 1.0
+        sent = float(torch.tensor(sent, dtype=torch.float32))
+
+        def kern():
+            rc = lib.tm_jv_solve_f32(x.data_ptr(), b, n, m, ctypes.c_float(sent), 1,
+                                     out.data_ptr(), ws.data_ptr(), stream)
+            assert rc == 0, lib.tm_status_string(rc)
+        kname = "jv_batch_kernel (sentinel solve; the op runs a check-mode pass first)"
+    else:
+        def kern():
+            rc = lib.tm_jv_solve_checked_f32(x.data_ptr(), b, n, m, out.data_ptr(),
+                                             ws.data_ptr(), stream)
+            assert rc == 0, lib.tm_status_string(rc)
+        kname = "jv_batch_kernel (check mode; the op's only launch)"
+    k_ms = _device_ms(kern, steps, 1)
+    del x, out
+    torch.cuda.empty_cache()
+    alg = b * (n * m * 4 + n * 8)
+    rec = {"workload": spec["desc"], "B": b, "value": b / (op_ms / 1e3), "unit": UNIT,
+           "ms_per_step": op_ms, "steps": steps,
+           "roofline": {"bound": "hbm", "kernel": kname, "avg_launch_us": k_ms * 1e3,
+                        "alg_bytes_per_launch": alg,
+                        "achieved": alg / (k_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                        "frac": alg / (k_ms / 1e3) / 1e9 / peak,
+                        "traffic": traffic_for(cfg)},
+           "gpu_launches_per_step": 2 if has_inf else 1}
+    if not args.no_cpu:
+        rec["cpu_baseline"] = cpu_baseline(cfg, seconds=3.0)
+    return rec
+
+
+def strong_c5_record(dev, world: int, rank: int, args) -> dict:
+    """Config 5 as strong scaling: the fixed B=65536 batch split into
+    `world` contiguous slices, one per rank (each generated on its GPU),
+    solved by sharded.solve_sharded (one all-reduce of the statistics words,
+    then the local solve) every step; max over ranks of the CUDA-event time."""
+    import torch
+    import torch.distributed as dist
+
+    from torchmatch_b200 import sharded
+
+    spec = CONFIGS["c5"]
+    b = spec["B"] // world
+    x = make_batch_device("c5", b, 500 + rank, dev).contiguous()
+    steps = 3
+    step = (lambda: sharded.solve_sharded(x)) if world > 1 else \
+        (lambda: torch.ops.assignment.jonker_dense_batch(x))
+    step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del x
+    torch.cuda.empty_cache()
+    return {"workload": spec["desc"], "global_batch": spec["B"], "per_gpu_batch": b,
+            "n_gpus": world, "scaling": "strong", "value": spec["B"] / (ms / 1e3),
+            "unit": UNIT, "ms_per_step": ms, "steps": steps,
+            "timing": "CUDA events per rank, max over ranks"}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -473,6 +591,11 @@ def run_ours(args):
            "problems_per_step": eb * world}
 
     base = cpu_baseline(args.config) if (rank == 0 and world == 1) else None
+    per_config = None
+    if world == 1 and not args.no_per_config:
+        per_config = {c: per_config_record(c, dev, lib, args, peak)
+                      for c in ("c1", "c3", "c4", "c5")}
+    strong = strong_c5_record(dev, world, rank, args) if not args.no_per_config else None
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -491,6 +614,8 @@ def run_ours(args):
             "cpu_baseline": base,
             "e2e": e2e,
             "pipelined": pipelined,
+            "per_config": per_config,
+            "strong_c5": strong,
             "gpu_launches": args.steps,  # one check-mode solve per step (no +inf)
             "clocks": clk if clocks else None,
         }
@@ -715,6 +840,10 @@ def main():
                     help="streams of the pipelined (async op) measurement")
     ap.add_argument("--scatter", action="store_true",
                     help="one process over every visible GPU, batch scattered from cuda:0")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="skip the per-config records and the config-5 strong-scaling leg")
+    ap.add_argument("--no-cpu", action="store_true",
+                    help="skip the CPU baselines of the per-config records")
     ap.add_argument("--fused", action="store_true",
                     help="fused squared-Euclidean cost construction on config-5 point sets")
     args = ap.parse_args()

@@ -651,16 +651,18 @@ __device__ __forceinline__ bool arr_direct(const float *__restrict__ src, const 
                 const unsigned h1 = head + 1, vis1 = visits + 1;
                 const int queued = qnext;
                 // lane-local lexicographic (value, column) top-2; the slots
-                // of a lane ascend in column
+                // of a lane ascend in column.  Selects, not branches: the
+                // comparisons differ between lanes.
                 float a1 = c[0] - v[0], a2 = inf;
-                int c1 = jj[0], c2 = 0x7fffffff;
+                int c1 = jj[0];
 #pragma unroll
                 for (int t = 1; t < S; ++t) {
                     const float x = c[t] - v[t];
-                    if (x < a1) { a2 = a1; c2 = c1; a1 = x; c1 = jj[t]; }
-                    else if (x < a2) { a2 = x; c2 = jj[t]; }
+                    const bool lt1 = x < a1;
+                    a2 = lt1 ? a1 : fminf(a2, x);
+                    a1 = lt1 ? x : a1;
+                    c1 = lt1 ? jj[t] : c1;
                 }
-                (void)c2;
                 const float v1 = warp_min_f(a1);
                 const int j1 = (int)warp_min_u_ord(a1 == v1 ? (unsigned)c1 : 0xffffffffu);
                 const int i0 = lds_s16(w.ycol + j1);
@@ -719,8 +721,11 @@ __device__ __forceinline__ bool arr_direct(const float *__restrict__ src, const 
 #pragma unroll
             for (int t = 1; t < S; ++t) {
                 const float x = c[t] - v[t];
-                if (x < a1) { a2 = a1; c2 = c1; a1 = x; c1 = jj[t]; }
-                else if (x < a2) { a2 = x; c2 = jj[t]; }
+                const bool lt1 = x < a1, lt2 = x < a2;
+                a2 = lt1 ? a1 : (lt2 ? x : a2);
+                c2 = lt1 ? c1 : (lt2 ? jj[t] : c2);
+                a1 = lt1 ? x : a1;
+                c1 = lt1 ? jj[t] : c1;
             }
             float v1 = warp_min_f(a1);
             int j1 = (int)warp_min_u(a1 == v1 ? (unsigned)c1 : 0xffffffffu);
@@ -1089,9 +1094,14 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     int c1 = jj[0], c2 = 0x7fffffff;
 #pragma unroll
                     for (int t = 1; t < S; ++t) {
+                        // selects, not branches: the comparisons differ
+                        // between lanes
                         const float x = c[t] - v[t];
-                        if (x < a1) { a2 = a1; c2 = c1; a1 = x; c1 = jj[t]; }
-                        else if (x < a2) { a2 = x; c2 = jj[t]; }
+                        const bool lt1 = x < a1, lt2 = x < a2;
+                        a2 = lt1 ? a1 : (lt2 ? x : a2);
+                        c2 = lt1 ? c1 : (lt2 ? jj[t] : c2);
+                        a1 = lt1 ? x : a1;
+                        c1 = lt1 ? jj[t] : c1;
                     }
                     v1 = warp_min_f(a1);
                     const bool at1 = a1 == v1;
