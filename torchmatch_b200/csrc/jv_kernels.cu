@@ -115,10 +115,16 @@ __host__ __device__ inline float key_to_float(uint32_t k) {
 #endif
 }
 
+// Cell classes and the largest finite cell, by integer selects (no branch:
+// the classes differ between lanes).
 __device__ __forceinline__ void classify(float x, uint32_t &fl, uint32_t &mk) {
-    if (isnan(x)) fl |= TM_STAT_NAN;
-    else if (isinf(x)) fl |= x < 0.0f ? TM_STAT_NEG_INF : TM_STAT_POS_INF;
-    else { fl |= TM_STAT_FINITE; mk = max(mk, order_key(x)); }
+    const uint32_t u = __float_as_uint(x);
+    const uint32_t a = u & 0x7fffffffu;
+    const bool finite = a < 0x7f800000u;
+    const uint32_t nonfin = a > 0x7f800000u ? TM_STAT_NAN
+                                           : ((u >> 31) ? TM_STAT_NEG_INF : TM_STAT_POS_INF);
+    fl |= finite ? TM_STAT_FINITE : nonfin;
+    mk = finite ? max(mk, order_key(x)) : mk;
 }
 
 // ---------------------------------------------------------------- warp ops
@@ -152,6 +158,13 @@ __device__ __forceinline__ int lds_s16(const int16_t *p) {
 __device__ __forceinline__ float lds_f32(const float *p) {
     float r;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)));
+    return r;
+}
+__device__ __forceinline__ float2 lds_f32x2(const float2 *p) {
+    float2 r;
+    asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];"
+                 : "=f"(r.x), "=f"(r.y)
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
     return r;
 }
 __device__ __forceinline__ void sts_s16(int16_t *p, int x) {
@@ -1016,7 +1029,60 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                                  : (unsigned)K * (unsigned)K + 2u * K + 8u;
         if (P.loop_bound && (unsigned)P.loop_bound < cap) cap = (unsigned)P.loop_bound;
         int row = w.queue[0];
+        const unsigned nf = (unsigned)nfree;
+        // cached mode: the queued row of the coming step, read ahead
+        int qnext = w.queue[1 < nf ? 1 : 0];
+        (void)qnext;
         while (head < (unsigned)nfree && visits < cap) {
+            if constexpr (use_cache) {
+                // ---- fast steps: a cache hit that needs neither the LARGE
+                // replay nor the j2 switch, in the ordered, branch-free form
+                // of arr_direct (prices and y are in shared memory here).
+                // A step that is not such a hit commits nothing and ends the
+                // fast loop; the general step below then runs it.
+                const float inf = __int_as_float(0x7f800000);
+                bool ok = true;
+                do {
+                    const unsigned h1 = head + 1, vis1 = visits + 1;
+                    const int queued = qnext;
+                    // every lane loads a candidate (lanes >= kCache repeat
+                    // one); only lanes < kCache offer theirs
+                    const float2 e = lds_f32x2(w.centry + row * kCache + (lane & (kCache - 1)));
+                    const float cb = lds_f32(w.cbound + row);
+                    const int cj = __float_as_int(e.y);
+                    const float vc = lds_f32(w.vsh + cj);
+                    const float cv = lane < kCache ? e.x - vc : inf;
+                    const float v1 = warp_min_f(cv);
+                    const int j1 = (int)warp_min_u_ord(cv == v1 ? (unsigned)cj : 0xffffffffu);
+                    const int i0 = lds_s16(w.ycol + j1);
+                    const float vj1 = lds_f32(w.vsh + j1);
+                    const float v2 = warp_min_f(cj == j1 ? inf : cv);
+                    const bool early = P.compact || vis1 < h1 * (unsigned)K;
+                    const float lowered = vj1 - (v2 - v1);
+                    const bool lowers = lowered < vj1;
+                    ok = v2 < cb && v2 < big2 && !(early && !lowers && i0 >= 0);
+                    const bool lower_now = early && lowers && ok;
+                    const bool push_front = i0 >= 0 && lower_now;
+                    const bool push_back = i0 >= 0 && !push_front && ok;
+                    // the same words from every lane; a step that is not
+                    // committed stores the old values back (vsh, ycol), a
+                    // free slot (queue) or a word its general step rewrites
+                    sts_f32(w.vsh + j1, lower_now ? lowered : vj1);
+                    sts_s16(w.ycol + j1, ok ? row : i0);
+                    sts_s32(w.xrow + row, j1);
+                    sts_s16(w.queue + kept, i0);
+                    kept += push_back;
+                    head = ok ? h1 - push_front : head;
+                    visits = ok ? vis1 : visits;
+                    row = ok ? (push_front ? i0 : queued) : row;
+                    qnext = lds_s16(w.queue + (head + 1 < nf ? head + 1 : 0));
+                } while (ok && head < nf && visits < cap);
+                __syncwarp();
+                if (ok) break;  // the pass ended inside the fast loop
+            }
+#ifdef TMJV_PHASE_CLOCKS
+            const long long t_gen = clock64();
+#endif
             ++visits;
             ++head;
             // the next queued row; push-backs only write consumed slots
@@ -1053,31 +1119,35 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     // lexicographic top-(kCache+1) by repeated extraction:
                     // ranks 0-1 answer this step, ranks 0..kCache-1 are
                     // cached, rank kCache bounds every uncached column
-                    unsigned gone = 0;
+                    // reduced costs once; taken (and padding) slots turn +inf
+                    // (a real reduced cost is finite), and each lane offers
+                    // its first smallest slot by selects
+                    float x[S];
+#pragma unroll
+                    for (int t = 0; t < S; ++t)
+                        x[t] = (valid >> t & 1) ? c[t] - v[t] : __int_as_float(0x7f800000);
                     float rk[kCache + 1];
                     int jk[kCache + 1];
 #pragma unroll
                     for (int k = 0; k <= kCache; ++k) {
-                        float a = __int_as_float(0x7f800000);
-                        int sa = -1;
+                        float a = x[0];
+                        int sa = 0;
 #pragma unroll
-                        for (int t = 0; t < S; ++t) {
-                            const float x = c[t] - v[t];
-                            if (!(gone >> t & 1) && (valid >> t & 1) && (sa < 0 || x < a)) {
-                                a = x;
-                                sa = t;
-                            }
+                        for (int t = 1; t < S; ++t) {
+                            const bool lt = x[t] < a;
+                            a = lt ? x[t] : a;
+                            sa = lt ? t : sa;
                         }
-                        const int ja = sa >= 0 ? L::col(sa, lane) : 0x7fffffff;
+                        const bool any = a < __int_as_float(0x7f800000);
+                        const int ja = any ? L::col(sa, lane) : 0x7fffffff;
                         const float m = warp_min_f(a);
-                        const int jm = (int)warp_min_u(sa >= 0 && a == m ? (unsigned)ja
-                                                                         : 0xffffffffu);
-                        if (ja == jm) {
-                            gone |= 1u << sa;
-                            if (k < kCache)
-                                w.centry[row * kCache + k] =
-                                    make_float2(sel(c, sa), __int_as_float(jm));
-                        }
+                        const int jm = (int)warp_min_u(any && a == m ? (unsigned)ja : 0xffffffffu);
+                        const bool won = ja == jm;
+                        if (k < kCache && won)
+                            w.centry[row * kCache + k] = make_float2(sel(c, sa), __int_as_float(jm));
+#pragma unroll
+                        for (int t = 0; t < S; ++t)
+                            x[t] = (won && t == sa) ? __int_as_float(0x7f800000) : x[t];
                         rk[k] = m;
                         jk[k] = jm;
                     }
@@ -1204,6 +1274,17 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             // a hit only stores words that every lane writes itself; a miss
             // wrote per-lane cache entries that other lanes read later
             if (use_cache && !hit) __syncwarp();
+            if constexpr (use_cache) {
+                __syncwarp();
+                qnext = w.queue[head + 1 < nf ? head + 1 : 0];
+            }
+#ifdef TMJV_PHASE_CLOCKS
+            if (lane == 0) {
+                atomicAdd(&tmjv_phase_cycles[17], 1ull);
+                atomicAdd(&tmjv_phase_cycles[18], (unsigned long long)(clock64() - t_gen));
+                atomicAdd(&tmjv_phase_cycles[19], hit ? 0ull : 1ull);
+            }
+#endif
         }
 #ifdef TMJV_PHASE_CLOCKS
         if (lane == 0) atomicAdd(&tmjv_phase_cycles[5], (unsigned long long)visits);
