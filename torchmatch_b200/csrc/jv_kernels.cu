@@ -155,6 +155,15 @@ __device__ __forceinline__ int lds_s16(const int16_t *p) {
     asm volatile("ld.shared.s16 %0, [%1];" : "=r"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)));
     return r;
 }
+// `old`, or the 16-bit word at p when `pred` holds: one predicated load.
+__device__ __forceinline__ int lds_s16_if(bool pred, const int16_t *p, int old) {
+    int r;
+    asm volatile(
+        "{ .reg .pred q; setp.ne.b32 q, %2, 0; mov.b32 %0, %3; @q ld.shared.s16 %0, [%1]; }"
+        : "=r"(r)
+        : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"((int)pred), "r"(old));
+    return r;
+}
 __device__ __forceinline__ float lds_f32(const float *p) {
     float r;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)));
@@ -658,9 +667,15 @@ __device__ __forceinline__ bool arr_direct(const float *__restrict__ src, const 
         row_of(row, c);
         __syncwarp();
         while (head < nf && visits < cap) {
-            bool rare = false;
-            // ---- fast steps
+            // ---- fast steps.  A step commits only while the pass is live
+            // (head < nf, visits below the cap) and the step before it was
+            // not rare; the loop branch tests that flag, which is known at
+            // the top of the step, so it never waits for the step's own
+            // decisions.  A rare step commits nothing, so the step after it
+            // repeats the same state without committing and the loop ends.
+            bool rare = false, live;
             do {
+                live = head < nf && visits < cap && !rare;
                 const unsigned h1 = head + 1, vis1 = visits + 1;
                 const int queued = qnext;
                 // lane-local lexicographic (value, column) top-2; the slots
@@ -684,46 +699,38 @@ __device__ __forceinline__ bool arr_direct(const float *__restrict__ src, const 
                 float cn[S], cq[S];
                 if constexpr (kMask) row_of(i0 & (K - 1), cn);
                 else row_of(i0 >= 0 ? i0 : row, cn);
-                if constexpr (TILE) row_of(queued, cq);
+                row_of(queued, cq);
                 // rr_cnt < current * n (absent from the compact variant)
                 const bool early = compact || vis1 < h1 * (unsigned)K;
                 const float lowered = vj1 - (v2 - v1);
                 const bool lowers = lowered < vj1;
                 rare = !(v2 < big2) || (early && !lowers && i0 >= 0);
-                const bool lower_now = early && lowers && !rare;
+                const bool commit = live && !rare;
+                const bool lower_now = early && lowers && commit;
                 const bool push_front = i0 >= 0 && lower_now;
-                const bool push_back = i0 >= 0 && !push_front && !rare;
-                // every lane stores the same words; a rare step stores
-                // the old values back (ycol, vsh), a slot that is free
-                // (queue) or a word the rare step rewrites (xrow)
+                const bool push_back = i0 >= 0 && !push_front && commit;
+                // every lane stores the same words; a step that does not
+                // commit stores the old values back (vsh, ycol) or a slot
+                // past the kept entries (queue).  x is not kept here: it is
+                // rebuilt from y when the phase ends.
                 sts_f32(vsh + j1, lower_now ? lowered : vj1);
 #pragma unroll
                 for (int t = 0; t < S; ++t) v[t] = (lower_now && jj[t] == j1) ? lowered : v[t];
-                sts_s16(w.ycol + j1, rare ? i0 : row);
-                sts_s32(w.xrow + row, j1);
+                sts_s16(w.ycol + j1, commit ? row : i0);
                 sts_s16(w.queue + kept, i0);
                 kept += push_back;
-                head = rare ? head : h1 - push_front;
-                visits = rare ? visits : vis1;
-                const int nrow = push_front ? i0 : queued;
-                qnext = lds_s16(w.queue + (head + 1 < nf ? head + 1 : 0));
-                if constexpr (TILE) {
+                head = commit ? h1 - push_front : head;
+                visits = commit ? vis1 : visits;
+                // the queued row moves on only after a step that consumed it
+                qnext = lds_s16_if(commit && !push_front,
+                                   w.queue + (h1 + 1 < nf ? h1 + 1 : 0), qnext);
 #pragma unroll
-                    for (int t = 0; t < S; ++t) c[t] = rare ? c[t] : (push_front ? cn[t] : cq[t]);
-                    row = rare ? row : nrow;
-                } else {
-                    if (!rare) {
-                        row = nrow;
-                        if (push_front) {
-#pragma unroll
-                            for (int t = 0; t < S; ++t) c[t] = cn[t];
-                        } else {
-                            row_of(row, c);
-                        }
-                    }
-                }
-            } while (!rare && head < nf && visits < cap);
-            if (!rare) break;
+                for (int t = 0; t < S; ++t) c[t] = commit ? (push_front ? cn[t] : cq[t]) : c[t];
+                row = commit ? (push_front ? i0 : queued) : row;
+            } while (live);
+            // the loop ended at the pass end, or on a rare step (which then
+            // runs below)
+            if (!(head < nf && visits < cap)) break;
             // ---- one general step on `row` (uncommitted by the fast loop)
             __syncwarp();
             ++visits;
@@ -795,7 +802,6 @@ __device__ __forceinline__ bool arr_direct(const float *__restrict__ src, const 
                 for (int t = 0; t < S; ++t) v[t] = jj[t] == j1 ? lowered : v[t];
             }
             w.ycol[jsel] = (int16_t)row;
-            w.xrow[row] = jsel;
             if (push_back) w.queue[kept] = (int16_t)i0;
             kept += push_back;
             head -= push_front;
@@ -812,6 +818,17 @@ __device__ __forceinline__ bool arr_direct(const float *__restrict__ src, const 
         nfree = kept;
         __syncwarp();
     }
+    // x of every assigned row from y (x[i] = j exactly when y[j] = i).  Rows
+    // left free keep a stale x, as in the reference: the augmentation reads
+    // x only for rows that own a column (the free start row's x is read and
+    // discarded, jonker_dense_flat.h:244-255).
+#pragma unroll
+    for (int s = 0; s < S; ++s)
+        if (valid >> s & 1) {
+            const int r = w.ycol[jj[s]];
+            if (r >= 0) w.xrow[r] = jj[s];
+        }
+    __syncwarp();
     return failed;
 }
 
@@ -1466,15 +1483,16 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 unsigned ev = 0;
 #pragma unroll
                 for (int s = 0; s < S; ++s) {
-                    if (todo >> s & 1) {
-                        const float rr = c[s] - v[s] - h;
-                        if (rr < d[s]) {
-                            d[s] = rr;
-                            w.dist[jj[s]] = rr;
-                            w.pred[jj[s]] = (int16_t)i;
-                            if (rr == dj) ev |= 1u << s;
-                        }
+                    // selects and predicated stores: the updates differ
+                    // between lanes
+                    const float rr = c[s] - v[s] - h;
+                    const bool upd = (todo >> s & 1) && rr < d[s];
+                    d[s] = upd ? rr : d[s];
+                    if (upd) {
+                        w.dist[jj[s]] = rr;
+                        w.pred[jj[s]] = (int16_t)i;
                     }
+                    ev |= (upd && rr == dj) ? 1u << s : 0u;
                 }
                 if (!__any_sync(kFull, ev != 0)) continue;
                 // tie events: order them by position
