@@ -13,8 +13,9 @@ spread one batch over several GPUs:
   crosses between GPUs.
 * ``solve_multi_gpu(costs, devices)`` -- one process driving several GPUs:
   contiguous slices are peer-copied (NVLink) from the caller's device to
-  each GPU on that GPU's own stream, solved there, and the int64 results are
-  copied back into one output on the caller's device.
+  each GPU in pieces, each piece solved as soon as it has arrived while the
+  next one crosses the link, and the int64 results are copied back into one
+  output on the caller's device.
 
 Both produce exactly what ``torch.ops.assignment.jonker_dense_batch`` gives
 on the whole batch.  ``solve_points_sharded`` is the one-process-per-GPU
@@ -31,6 +32,7 @@ import torch
 from torchmatch_b200 import _loader
 
 _NAN, _NEG_INF, _FINITE, _POS_INF = 1, 2, 4, 8
+_WS_TIMEOUT, _ERR_TIMEOUT = 8, 7  # TM_WS_TIMEOUT, TM_ERR_TIMEOUT
 
 
 class _Stats(ctypes.Structure):
@@ -71,30 +73,6 @@ def order_key(x: float) -> int:
 
 def _stream(dev: torch.device) -> int:
     return torch.cuda.current_stream(dev).cuda_stream
-
-
-def _local_stats(c: torch.Tensor) -> list[int]:
-    lib = _loader.core()
-    st = torch.empty(lib.tm_jv_workspace_bytes() // 4, dtype=torch.int32, device=c.device)
-    rc = lib.tm_jv_stats_f32(c.data_ptr(), c.numel(), st.data_ptr(), _stream(c.device))
-    if rc != 0:
-        raise RuntimeError("jonker_dense_batch statistics: " + lib.tm_status_string(rc).decode())
-    flags, key = (int(v) & 0xFFFFFFFF for v in st[:2].cpu().tolist())
-    return stats_words(flags, key)
-
-
-def _solve_local(c: torch.Tensor, sentinel: float, pinf: bool) -> torch.Tensor:
-    lib = _loader.core()
-    b, n, m = c.shape
-    out = torch.empty(b, n, dtype=torch.long, device=c.device)
-    if b == 0 or n == 0:
-        return out
-    ws = torch.empty(lib.tm_jv_workspace_bytes(), dtype=torch.uint8, device=c.device)
-    rc = lib.tm_jv_solve_f32(c.data_ptr(), b, n, m, sentinel, int(pinf), out.data_ptr(),
-                             ws.data_ptr(), _stream(c.device))
-    if rc != 0:
-        raise RuntimeError("batched JV kernel launch failed: " + lib.tm_status_string(rc).decode())
-    return out
 
 
 def merge_words(words: list[int], group=None, device=None) -> list[int]:
@@ -212,17 +190,30 @@ def solve_points_sharded(x_local: torch.Tensor, y_local: torch.Tensor, group=Non
     return out
 
 
-_PEER_STREAMS: dict[int, torch.cuda.Stream] = {}
+_PEER_STREAMS: dict[tuple[int, str], torch.cuda.Stream] = {}
+_WORKSPACES: dict[int, torch.Tensor] = {}
 
 
-def _peer_stream(dev: torch.device) -> torch.cuda.Stream:
-    """One long-lived stream per GPU for solve_multi_gpu.  The caching
-    allocator keeps freed blocks per stream, so a fresh stream per call would
-    allocate every slice anew (and free the cache, which synchronises the
-    device, once memory runs short)."""
-    if dev.index not in _PEER_STREAMS:
-        _PEER_STREAMS[dev.index] = torch.cuda.Stream(dev)
-    return _PEER_STREAMS[dev.index]
+def _peer_stream(dev: torch.device, role: str) -> torch.cuda.Stream:
+    """Long-lived streams per GPU for solve_multi_gpu (a copy stream and two
+    solve streams).  The caching allocator keeps freed blocks per stream, so
+    a fresh stream per call would allocate every slice anew (and free the
+    cache, which synchronises the device, once memory runs short)."""
+    key = (dev.index, role)
+    if key not in _PEER_STREAMS:
+        _PEER_STREAMS[key] = torch.cuda.Stream(dev)
+    return _PEER_STREAMS[key]
+
+
+def _workspaces(dev: torch.device, count: int) -> torch.Tensor:
+    """`count` solve workspaces (one tm_jv_workspace each) on `dev`, kept
+    across calls and grown on demand."""
+    words = _loader.core().tm_jv_workspace_bytes() // 4
+    ws = _WORKSPACES.get(dev.index)
+    if ws is None or ws.shape[0] < count:
+        ws = torch.zeros(max(count, 16), words, dtype=torch.int32, device=dev)
+        _WORKSPACES[dev.index] = ws
+    return ws
 
 
 def shard_bounds(b: int, parts: int) -> list[tuple[int, int]]:
@@ -231,12 +222,30 @@ def shard_bounds(b: int, parts: int) -> list[tuple[int, int]]:
     return [(min(g * step, b), min((g + 1) * step, b)) for g in range(parts)]
 
 
-def solve_multi_gpu(costs: torch.Tensor, devices: list[int] | None = None) -> torch.Tensor:
+def _launch(lib, fn: str, *args) -> None:
+    rc = getattr(lib, fn)(*args)
+    if rc != 0:
+        raise RuntimeError("batched JV kernel launch failed: " + lib.tm_status_string(rc).decode())
+
+
+def solve_multi_gpu(costs: torch.Tensor, devices: list[int] | None = None,
+                    chunks: int = 4) -> torch.Tensor:
     """Solve one batch on several GPUs from a single process.
 
     ``costs`` lives on one CUDA device (the caller's); the result comes back
-    there.  Slices travel by peer copies on each target GPU's stream; the
-    statistics pass runs once on the caller's device.
+    there.  The batch is split into contiguous slices, one per device, and
+    every slice into ``chunks`` pieces.  On each GPU a copy stream brings the
+    pieces over NVLink one after another while two solve streams take turns
+    solving the pieces that have arrived, in check mode (each piece into its
+    own workspace), so piece k + 1 crosses the link while piece k is solved
+    and a piece's last problems overlap the next piece's first.  There is no
+    separate statistics pass: after one host read of every piece's
+    statistics (the reference raises on NaN / -inf after one host check as
+    well, cuda/cuda_common.cuh:245-249), a batch holding +inf is solved again
+    slice by slice with the global sentinel, from the slices already on their
+    GPUs.  The int64 results go back to the caller's device on the copy
+    streams.  The result equals ``torch.ops.assignment.jonker_dense_batch``
+    on the whole batch.
     """
     if costs.device.type != "cuda" or costs.dim() != 3:
         raise RuntimeError("costs must be a 3D CUDA tensor")
@@ -248,36 +257,70 @@ def solve_multi_gpu(costs: torch.Tensor, devices: list[int] | None = None) -> to
     k = max(n, m)
     if b == 0 or n == 0 or m == 0:
         return torch.full((b, n), -1, dtype=torch.long, device=home)
-    if k > _loader.core().tm_jv_max_k():
+    lib = _loader.core()
+    if k > lib.tm_jv_max_k():
         raise RuntimeError(f"Batched JV (CUDA) supports max(N, M) <= 256, got K={k}")
-    sentinel, pinf = sentinel_from_words(_local_stats(c), k)
     out = torch.empty(b, n, dtype=torch.long, device=home)
     home_stream = torch.cuda.current_stream(home)
     ready = torch.cuda.Event()
     ready.record(home_stream)
-    done = []
-    local = None
+    jobs = []
     for (lo, hi), d in zip(shard_bounds(b, len(devices)), devices):
         if hi <= lo:
             continue
         dev = torch.device("cuda", d)
-        if dev == home:
-            local = (lo, hi)  # solved last, after the peers are under way
-            continue
-        s = _peer_stream(dev)
-        with torch.cuda.device(dev), torch.cuda.stream(s):
-            s.wait_event(ready)
-            c.record_stream(s)  # s reads c: keep its block until s is done
-            part = c[lo:hi].to(dev, non_blocking=True)
-            res = _solve_local(part, sentinel, pinf)
-            ev = torch.cuda.Event()
-            ev.record(s)
-            done.append((ev, res, lo, hi))
-    if local is not None:
-        lo, hi = local
-        out[lo:hi] = _solve_local(c[lo:hi], sentinel, pinf)
-    for ev, res, lo, hi in done:
-        home_stream.wait_event(ev)
-        out[lo:hi].copy_(res, non_blocking=True)
-        res.record_stream(home_stream)  # read by the home stream after s
+        pieces = [(p0, p1) for p0, p1 in shard_bounds(hi - lo, max(1, chunks)) if p1 > p0]
+        ws = _workspaces(dev, len(pieces))
+        cs = _peer_stream(dev, "copy")
+        solvers = (_peer_stream(dev, "solve0"), _peer_stream(dev, "solve1"))
+        with torch.cuda.device(dev), torch.cuda.stream(cs):
+            cs.wait_event(ready)
+            for st in solvers:
+                st.wait_stream(cs)  # earlier users of this GPU's workspaces are done
+            if dev == home:
+                part = c[lo:hi]
+                c.record_stream(solvers[0])
+                c.record_stream(solvers[1])
+            else:
+                part = torch.empty(hi - lo, n, m, dtype=torch.float32, device=dev)
+                c.record_stream(cs)  # cs reads c: keep its block until cs is done
+            res = torch.empty(hi - lo, n, dtype=torch.long, device=dev)
+            for q, (p0, p1) in enumerate(pieces):
+                st = solvers[q % 2]
+                if dev != home:
+                    part[p0:p1].copy_(c[lo + p0:lo + p1], non_blocking=True)
+                    arrived = torch.cuda.Event()
+                    arrived.record(cs)
+                    st.wait_event(arrived)
+                _launch(lib, "tm_jv_solve_checked_f32", part[p0:].data_ptr(), p1 - p0, n, m,
+                        res[p0:].data_ptr(), ws[q].data_ptr(), st.cuda_stream)
+            for st in solvers:
+                cs.wait_stream(st)
+                part.record_stream(st)
+                res.record_stream(st)
+        jobs.append((dev, part, res, lo, hi, ws[:len(pieces)]))
+    # one host read of every piece's statistics and status, after its solves
+    flags, key = 0, 0
+    for dev, part, res, lo, hi, ws in jobs:
+        torch.cuda.current_stream(dev).wait_stream(_peer_stream(dev, "copy"))
+        with torch.cuda.device(dev):
+            # words 0, 1: tm_jv_stats; word 4: the status (TM_WS_* bits)
+            for f, kk, status in ws[:, [0, 1, 4]].cpu().tolist():
+                flags |= int(f) & 0xFFFFFFFF
+                key = max(key, int(kk) & 0xFFFFFFFF)
+                if status & _WS_TIMEOUT:
+                    raise RuntimeError("jonker_dense_batch: "
+                                       + lib.tm_status_string(_ERR_TIMEOUT).decode())
+    sentinel, pinf = sentinel_from_words(stats_words(flags, key), k)
+    for dev, part, res, lo, hi, ws in jobs:
+        cs = _peer_stream(dev, "copy")
+        with torch.cuda.device(dev), torch.cuda.stream(cs):
+            if pinf:
+                _launch(lib, "tm_jv_solve_f32", part.data_ptr(), hi - lo, n, m, sentinel, 1,
+                        res.data_ptr(), ws[0].data_ptr(), cs.cuda_stream)
+            out[lo:hi].copy_(res, non_blocking=True)
+            out.record_stream(cs)
+            done = torch.cuda.Event()
+            done.record(cs)
+        home_stream.wait_event(done)
     return out
