@@ -811,19 +811,46 @@ def run_scatter(args):
 
 
 def run_once(args):
-    """Two calls of the op on one resident batch, nothing timed: the case the
-    committed ncu summaries under profiles/ were captured on."""
+    """Two calls of one entry point on one resident batch, nothing timed: the
+    cases the committed ncu summaries under profiles/ were captured on.
+    --op dense: jonker_dense_batch; async: jonker_dense_batch_async (check
+    launch + gated launch); stats: the standalone statistics kernel through
+    the C ABI; fused: jonker_sqeuclidean_batch on config-5 point sets."""
     import torch
 
     import torchmatch_b200  # noqa: F401
+    from torchmatch_b200 import _loader
 
+    dev = torch.device("cuda")
     spec = CONFIGS[args.config]
     b = args.batch or spec["B"]
-    x = make_batch_device(args.config, b, 0, torch.device("cuda"))
+    if args.op == "fused":
+        g = torch.Generator(device=dev).manual_seed(1)
+        px = torch.randn(b, 256, 16, device=dev, generator=g)
+        py = torch.randn(b, 256, 16, device=dev, generator=g)
+        for _ in range(2):
+            out = torch.ops.assignment.jonker_sqeuclidean_batch(px, py)
+        torch.cuda.synchronize()
+        print("once fused", tuple(px.shape), tuple(out.shape))
+        return
+    x = make_batch_device(args.config, b, 0, dev)
+    if args.op == "stats":
+        lib = _loader.core()
+        st = torch.zeros(lib.tm_jv_workspace_bytes() // 4, dtype=torch.int32, device=dev)
+        for _ in range(2):
+            rc = lib.tm_jv_stats_f32(x.data_ptr(), x.numel(), st.data_ptr(),
+                                     torch.cuda.current_stream().cuda_stream)
+            assert rc == 0, lib.tm_status_string(rc)
+        torch.cuda.synchronize()
+        print("once stats", args.config, tuple(x.shape))
+        return
     for _ in range(2):
-        out = torch.ops.assignment.jonker_dense_batch(x)
+        if args.op == "async":
+            out = torch.ops.assignment.jonker_dense_batch_async(x)[0]
+        else:
+            out = torch.ops.assignment.jonker_dense_batch(x)
     torch.cuda.synchronize()
-    print("once", args.config, tuple(x.shape), tuple(out.shape))
+    print("once", args.op, args.config, tuple(x.shape), tuple(out.shape))
 
 
 def main():
@@ -836,6 +863,8 @@ def main():
     ap.add_argument("--once", action="store_true",
                     help="solve the workload twice and exit (a small case for ncu captures)")
     ap.add_argument("--batch", type=int, default=0, help="override B (with --once / --fused)")
+    ap.add_argument("--op", default="dense", choices=["dense", "async", "stats", "fused"],
+                    help="entry point of --once")
     ap.add_argument("--streams", type=int, default=3,
                     help="streams of the pipelined (async op) measurement")
     ap.add_argument("--scatter", action="store_true",
