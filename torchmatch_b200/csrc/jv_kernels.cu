@@ -1354,62 +1354,66 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 if (lo >= K) { failed = true; break; }
                 ready |= grp;
                 grp = 0;
-                float dv[S];
+                // Positions are scanned lane-major here (lane l holds
+                // positions l*S .. l*S+S-1), so the running minimum inside a
+                // lane is sequential and one warp scan of the lane minima
+                // (plus one of the event counts) replaces S interleaved scans.
                 const float inf = __int_as_float(0x7f800000);
+                float dv[S];
 #pragma unroll
                 for (int s = 0; s < S; ++s) {
-                    const int p = s * 32 + lane;
-                    dv[s] = inf;
-                    if (p >= lo && p < K) dv[s] = w.dist[w.order[p]];
+                    const int p = lane * S + s;
+                    dv[s] = (p >= lo && p < K) ? w.dist[w.order[p < K ? p : 0]] : inf;
                 }
-                // prefix minima over positions: the S per-slot scans are
-                // independent (run interleaved), then chained by their totals
-                float incl[S];
+                float lmin[S];
+                lmin[0] = dv[0];
 #pragma unroll
-                for (int s = 0; s < S; ++s) incl[s] = dv[s];
+                for (int s = 1; s < S; ++s) lmin[s] = fminf(lmin[s - 1], dv[s]);
+                float incl = lmin[S - 1];
 #pragma unroll
                 for (int off = 1; off < 32; off <<= 1) {
-#pragma unroll
-                    for (int s = 0; s < S; ++s) {
-                        const float t = __shfl_up_sync(kFull, incl[s], off);
-                        if (lane >= off) incl[s] = fminf(incl[s], t);
-                    }
+                    const float t = __shfl_up_sync(kFull, incl, off);
+                    incl = lane >= off ? fminf(incl, t) : incl;
                 }
-                float carry = inf;
-                unsigned evm[S], rsm[S];
+                float before = __shfl_up_sync(kFull, incl, 1);
+                before = lane == 0 ? inf : before;
+                mind = __shfl_sync(kFull, incl, 31);
+                // events: positions after lo whose d is at or below the
+                // running minimum of the positions before them (:31-41)
+                unsigned evb = 0, rsb = 0;
 #pragma unroll
                 for (int s = 0; s < S; ++s) {
-                    const int p = s * 32 + lane;
-                    float excl = __shfl_up_sync(kFull, incl[s], 1);
-                    excl = lane == 0 ? carry : fminf(carry, excl);
+                    const int p = lane * S + s;
+                    const float excl = s == 0 ? before : fminf(before, lmin[s - 1]);
                     const bool live = p > lo && p < K;
-                    const bool rst = live && dv[s] < excl;
-                    const bool tie = live && dv[s] == excl;
-                    rsm[s] = __ballot_sync(kFull, rst);
-                    evm[s] = __ballot_sync(kFull, rst || tie);
-                    carry = fminf(carry, __shfl_sync(kFull, incl[s], 31));
+                    evb |= (live && dv[s] <= excl) ? 1u << s : 0u;
+                    rsb |= (live && dv[s] < excl) ? 1u << s : 0u;
                 }
-                mind = carry;
-                // compact the events (position, original column, reset?) in
-                // position order; columns at event positions are untouched
-                // until their own event, so they are read here in parallel
+                int cnt = __popc(evb), off0 = cnt;
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const int t = __shfl_up_sync(kFull, off0, off);
+                    off0 += lane >= off ? t : 0;
+                }
+                const int base = __shfl_sync(kFull, off0, 31);
+                off0 -= cnt;
                 {
-                    int base = 0;
+                    // compact the events (position, original column, reset?)
+                    // in position order; columns at event positions are
+                    // untouched until their own event, so they are read here
 #pragma unroll
                     for (int s = 0; s < S; ++s) {
-                        if (evm[s] >> lane & 1) {
-                            const int k = s * 32 + lane;
-                            const int slot = base + __popc(evm[s] & ((1u << lane) - 1));
-                            w.evbuf[slot] = k | ((int)w.order[k] << 9) |
-                                            ((int)(rsm[s] >> lane & 1) << 18);
+                        if (evb >> s & 1) {
+                            const int k = lane * S + s;
+                            w.evbuf[off0] = k | ((int)w.order[k] << 9) | ((int)(rsb >> s & 1) << 18);
+                            ++off0;
                         }
-                        base += __popc(evm[s]);
                     }
                     __syncwarp();
 #ifdef TMJV_PHASE_CLOCKS
                     if (lane == 0) {
                         unsigned nr = 0;
-                        for (int s = 0; s < S; ++s) nr += __popc(rsm[s]);
+                        nr = 0;
                         atomicAdd(&tmjv_phase_cycles[8], (unsigned long long)base);
                         atomicAdd(&tmjv_phase_cycles[9], (unsigned long long)nr);
                         atomicAdd(&tmjv_phase_cycles[10], 1ull);
@@ -1423,15 +1427,11 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                             const int evn = q + 1 < base ? w.evbuf[q + 1] : 0;
                             const int k = ev & 511;
                             const int16_t e = (int16_t)((ev >> 9) & 511);
-                            if (ev >> 18) {
-                                w.order[k] = w.order[lo];
-                                w.order[lo] = e;
-                                nh = lo + 1;
-                            } else {
-                                w.order[k] = w.order[nh];
-                                w.order[nh] = e;
-                                ++nh;
-                            }
+                            // a reset restarts the group at lo
+                            const int tgt = (ev >> 18) ? lo : nh;
+                            w.order[k] = w.order[tgt];
+                            w.order[tgt] = e;
+                            nh = tgt + 1;
                             ev = evn;
                         }
                     }
