@@ -50,14 +50,24 @@ def wait_lib():
     core.tm_jv_debug_set_wait_limit(-1)
 
 
-def test_tile_wait_timeout_is_reported(wait_lib, oracle_mod):
-    """A tile copy whose bounded wait runs out (the hook makes the first wait
-    give up at once) leaves every problem as a row of -1, sets TM_WS_TIMEOUT
-    (bit 8) in the async op's status and makes the synchronous op raise; the
-    copy itself still lands before the tile is reused, and resetting the
-    hook brings back exact results."""
+def _streamed_square(b):
+    g = torch.Generator().manual_seed(17)
+    return torch.rand(b, 128, 128, generator=g)
+
+
+@pytest.mark.parametrize("make", [lambda: config2(300), lambda: _streamed_square(200)],
+                         ids=["tile64", "ring128"])
+def test_tile_wait_timeout_is_reported(wait_lib, oracle_mod, make):
+    """A TMA copy whose bounded wait runs out (the hook makes the first wait
+    give up at once) -- a 64 x 64 problem's shared-memory tile, or a chunk of
+    a streamed 128 x 128 problem's column-reduction ring -- leaves every
+    problem as a row of -1, sets TM_WS_TIMEOUT (bit 8) in the async op's
+    status and makes the synchronous op raise; the copies in flight still
+    land before their shared memory is reused, and resetting the hook brings
+    back exact results."""
     lib = wait_lib
-    x = config2(300)  # 64 x 64 problems are staged in shared memory by TMA
+    x = make()
+    b, n, m = x.shape
     ref = oracle_mod.jonker_dense_batch(x.numpy())
     xd = x.cuda()
     lib.tm_jv_debug_set_wait_limit(0)
@@ -68,9 +78,9 @@ def test_tile_wait_timeout_is_reported(wait_lib, oracle_mod):
         torch.ops.assignment.jonker_dense_batch(xd)
     # through the C ABI: TM_ERR_TIMEOUT and rows of -1 over a poisoned buffer
     ws = torch.zeros(lib.tm_jv_workspace_bytes(), dtype=torch.uint8, device="cuda")
-    got = torch.full((300, 64), 7, dtype=torch.long, device="cuda")
+    got = torch.full((b, n), 7, dtype=torch.long, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
-    rc = lib.tm_jonker_dense_batch_f32(xd.data_ptr(), 300, 64, 64, got.data_ptr(),
+    rc = lib.tm_jonker_dense_batch_f32(xd.data_ptr(), b, n, m, got.data_ptr(),
                                        ws.data_ptr(), stream)
     assert rc == 7, lib.tm_status_string(rc)
     assert (got.cpu().numpy() == -1).all()

@@ -258,6 +258,43 @@ __device__ __forceinline__ void seti(int (&a)[S], int s, int x) {
         if (s == t) a[t] = x;
 }
 
+// --------------------------------------------------------- TMA primitives
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void bar_init(uint64_t *bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool bar_wait(uint64_t *bar, uint32_t phase, uint32_t limit) {
+    for (uint32_t it = 0; it < limit; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
+            "selp.u32 %0, 1, 0, p; }"
+            : "=r"(done)
+            : "r"(smem_u32(bar)), "r"(phase)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // --------------------------------------------------------------- smem view
 struct WarpShared {
     float *tile;       // staged (N, M) cost block (TILE mode)
@@ -275,9 +312,20 @@ struct WarpShared {
     float *cbound;     // [row]: lower bound of every uncached reduced cost
     uint8_t *cflag;    // [row]: cache built
     float *vsh;        // mirror of the prices v
+    // streamed rows: the column reduction's ring of kSlots slots of kChunk
+    // rows, filled by TMA bulk copies (it shares the row-cache area, unused
+    // until the augmenting row reduction), one mbarrier per slot, the parity
+    // each slot waits for next, and whether a copy ever failed to land (then
+    // the warp reads rows directly from then on)
+    float *ring;
+    uint64_t *rbar;
+    uint32_t rphase;
+    bool rdead;
 };
 
 constexpr int kCache = 4;  // cached columns per row
+constexpr int kSlots = 2;  // slots of the column reduction's TMA ring
+constexpr int kChunk = 4;  // rows per slot (one bulk copy)
 
 __host__ __device__ inline int slots_for(int K) { return (K + 31) / 32; }
 
@@ -285,7 +333,7 @@ __host__ __device__ inline int slots_for(int K) { return (K + 31) / 32; }
 __host__ __device__ inline int book_bytes(int KP, bool cache) {
     int b = KP * 4 /*dist*/ + KP * 4 /*xrow*/ + KP * 2 * 4 /*ycol,pred,queue,order*/ +
             KP /*flag*/ + KP * 4 /*evbuf*/ + 48 /*bar + alignment*/;
-    if (cache) b += KP * kCache * 8 + KP * 4 + KP * 4 + KP + 16;
+    if (cache) b += KP * kCache * 8 + KP * 4 + KP * 4 + KP + 16 + 8 * kSlots + 8;
     return b;
 }
 
@@ -310,8 +358,18 @@ __device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP,
         w.centry = reinterpret_cast<float2 *>(p); p += (size_t)KP * kCache * 8;
         w.cbound = reinterpret_cast<float *>(p); p += KP * 4;
         w.vsh = reinterpret_cast<float *>(p); p += KP * 4;
-        w.cflag = p;
+        w.cflag = p; p += KP;
+        p = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(p) + 7) & ~uintptr_t(7));
+        w.rbar = reinterpret_cast<uint64_t *>(p);
+        // kSlots * kChunk rows of KP floats: exactly the row-cache entries' bytes
+        static_assert(kSlots * kChunk * 4 == kCache * 8, "the ring must fit the row-cache area");
+        w.ring = reinterpret_cast<float *>(w.centry);
+    } else {
+        w.ring = nullptr;
+        w.rbar = nullptr;
     }
+    w.rphase = 0;
+    w.rdead = false;
     return w;
 }
 
@@ -867,7 +925,81 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     const float seed = P.compact ? __int_as_float(0x7f800000) : kBig;
 #pragma unroll
     for (int s = 0; s < S; ++s) { v[s] = seed; ymin[s] = 0; }
-    {
+    bool ring_used = false;
+    if constexpr (!TILE && !PTS && FULL) {
+        // Streamed square rows: the rows arrive through a ring of kSlots
+        // slots of kChunk rows in shared memory, each slot filled by one TMA
+        // bulk copy (cp.async.bulk + mbarrier), so the next chunk is in flight
+        // while the column minima of the current one are taken.  Chunk q (rows
+        // q*kChunk ..) goes to slot q % kSlots.  K is a multiple of 32, so
+        // every chunk is whole.
+        if (P.bulk_ok && !w.rdead) {
+            ring_used = true;
+            constexpr int KP = 32 * S;
+            constexpr int nchunk = KP / kChunk;
+            constexpr uint32_t cb = (uint32_t)(kChunk * KP * 4);
+            const bool check = P.check != 0;
+            __syncwarp();  // the previous problem's reads of this area are done
+            if (lane == 0) {
+                for (int q = 0; q < kSlots && q < nchunk; ++q)
+                    bulk_load(w.ring + q * (kChunk * KP), src + (int64_t)q * (kChunk * KP), cb,
+                              w.rbar + q);
+            }
+            bool ok = true;
+            int q = 0;
+            for (; q < nchunk; ++q) {
+                const int slot = q % kSlots;
+                ok = __all_sync(kFull, bar_wait(w.rbar + slot, (w.rphase >> slot) & 1u,
+                                                P.wait_limit));
+                if (!ok) break;
+                w.rphase ^= 1u << slot;
+                const float *chunk = w.ring + slot * (kChunk * KP);
+#pragma unroll
+                for (int r = 0; r < kChunk; ++r) {
+                    const int i = q * kChunk + r;
+                    load_row<S, VEC, true, FULL, false>(chunk, r, N, M, lane, false, sentinel, c);
+                    if (sanitize) {
+#pragma unroll
+                        for (int s = 0; s < S; ++s)
+                            if (isinf(c[s])) c[s] = sentinel;
+                    }
+#pragma unroll
+                    for (int s = 0; s < S; ++s) {
+                        const bool lt = c[s] < v[s];
+                        v[s] = lt ? c[s] : v[s];
+                        ymin[s] = lt ? i : ymin[s];
+                    }
+                    if (check) {
+#pragma unroll
+                        for (int s = 0; s < S; ++s) classify(c[s], chk_fl, chk_mk);
+                    }
+                }
+                __syncwarp();  // every lane has read the slot before it is refilled
+                if (lane == 0 && q + kSlots < nchunk)
+                    bulk_load(w.ring + slot * (kChunk * KP),
+                              src + (int64_t)(q + kSlots) * (kChunk * KP), cb, w.rbar + slot);
+            }
+            if (!ok) {
+                // A copy did not land in time: report it, let every copy in
+                // flight (chunks q .. q + kSlots - 1) land before the area is
+                // reused, and leave the problem as a row of -1.  If one never
+                // lands, this warp stops using the ring.
+                if (lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_WS_TIMEOUT);
+                for (int r = q; r < q + kSlots && r < nchunk; ++r) {
+                    const int slot = r % kSlots;
+                    if (__all_sync(kFull, bar_wait(w.rbar + slot, (w.rphase >> slot) & 1u,
+                                                   kWaitLimit)))
+                        w.rphase ^= 1u << slot;
+                    else
+                        w.rdead = true;
+                }
+                __syncwarp();
+                emit_result(P, w, lane, b, N, M, false);
+                return;
+            }
+        }
+    }
+    if (!ring_used) {
         const int nreal = N < K ? N : K;
         int i = 0;
         const bool check = P.check != 0;
@@ -1585,43 +1717,6 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     if (failed && lane == 0 && P.status) atomicOr(P.status, (int32_t)TM_WS_UNSOLVED);
 }
 
-// --------------------------------------------------------- TMA primitives
-__device__ __forceinline__ uint32_t smem_u32(const void *p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void bar_init(uint64_t *bar) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)));
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
-                                          uint64_t *bar) {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-            "r"(smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ bool bar_wait(uint64_t *bar, uint32_t phase, uint32_t limit) {
-    for (uint32_t it = 0; it < limit; ++it) {
-        uint32_t done;
-        asm volatile(
-            "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; "
-            "selp.u32 %0, 1, 0, p; }"
-            : "=r"(done)
-            : "r"(smem_u32(bar)), "r"(phase)
-            : "memory");
-        if (done) return true;
-    }
-    return false;
-}
-__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // ------------------------------------------------------------------ kernel
 template <int S, int VEC, bool TILE, bool FULL, bool PTS>
 __global__ void __launch_bounds__((TILE || S > 4 || PTS) ? 512 : 256, (TILE || S > 4 || PTS) ? 1 : 4) jv_batch_kernel(const Params P0) {
@@ -1654,6 +1749,10 @@ __global__ void __launch_bounds__((TILE || S > 4 || PTS) ? 512 : 256, (TILE || S
     uint32_t phase = 0;
     if constexpr (TILE) {
         if (lane == 0) bar_init(w.bar);
+        __syncwarp();
+    } else if constexpr (!PTS && FULL) {
+        if (lane == 0)
+            for (int r = 0; r < kSlots; ++r) bar_init(w.rbar + r);
         __syncwarp();
     }
     // Problems are claimed one at a time from a global ticket: the work per
