@@ -1262,9 +1262,19 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
             if (!hit) {
                 load_row<S, VEC, TILE, FULL, PTS>(src, row, N, M, lane, sanitize, sentinel, c);
                 if constexpr (use_cache) {
+                    if constexpr (FULL && VEC == 4) {
+                        // a lane's slots 4g .. 4g+3 are consecutive columns:
+                        // one conflict-free 16-byte load per group
 #pragma unroll
-                    for (int t = 0; t < S; ++t)
-                        if (valid >> t & 1) v[t] = w.vsh[jj[t]];
+                        for (int g = 0; g < S / 4; ++g) {
+                            const float4 q = *reinterpret_cast<const float4 *>(w.vsh + jj[4 * g]);
+                            v[4 * g] = q.x; v[4 * g + 1] = q.y; v[4 * g + 2] = q.z; v[4 * g + 3] = q.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int t = 0; t < S; ++t)
+                            if (valid >> t & 1) v[t] = w.vsh[jj[t]];
+                    }
                     // lexicographic top-(kCache+1) by repeated extraction:
                     // ranks 0-1 answer this step, ranks 0..kCache-1 are
                     // cached, rank kCache bounds every uncached column
