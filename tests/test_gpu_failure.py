@@ -52,15 +52,15 @@ def wait_lib():
 
 def _streamed_square(b):
     g = torch.Generator().manual_seed(17)
-    return torch.rand(b, 128, 128, generator=g)
+    return torch.rand(b, 256, 256, generator=g)
 
 
-@pytest.mark.parametrize("make", [lambda: config2(300), lambda: _streamed_square(200)],
-                         ids=["tile64", "ring128"])
+@pytest.mark.parametrize("make", [lambda: config2(300), lambda: _streamed_square(64)],
+                         ids=["tile64", "ring256"])
 def test_tile_wait_timeout_is_reported(wait_lib, oracle_mod, make):
     """A TMA copy whose bounded wait runs out (the hook makes the first wait
     give up at once) -- a 64 x 64 problem's shared-memory tile, or a chunk of
-    a streamed 128 x 128 problem's column-reduction ring -- leaves every
+    a streamed 256 x 256 problem's column-reduction ring -- leaves every
     problem as a row of -1, sets TM_WS_TIMEOUT (bit 8) in the async op's
     status and makes the synchronous op raise; the copies in flight still
     land before their shared memory is reused, and resetting the hook brings

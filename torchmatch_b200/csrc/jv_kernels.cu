@@ -926,7 +926,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
 #pragma unroll
     for (int s = 0; s < S; ++s) { v[s] = seed; ymin[s] = 0; }
     bool ring_used = false;
-    if constexpr (!TILE && !PTS && FULL) {
+    if constexpr (!TILE && !PTS && FULL && S >= 7) {
         // Streamed square rows: the rows arrive through a ring of kSlots
         // slots of kChunk rows in shared memory, each slot filled by one TMA
         // bulk copy (cp.async.bulk + mbarrier), so the next chunk is in flight
@@ -1729,7 +1729,7 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
 
 // ------------------------------------------------------------------ kernel
 template <int S, int VEC, bool TILE, bool FULL, bool PTS>
-__global__ void __launch_bounds__((TILE || S > 4 || PTS) ? 512 : 256, (TILE || S > 4 || PTS) ? 1 : 4) jv_batch_kernel(const Params P0) {
+__global__ void __launch_bounds__((TILE || S > 4 || PTS) ? 512 : 384, (TILE || S > 4 || PTS) ? 1 : 3) jv_batch_kernel(const Params P0) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     const int lane = threadIdx.x & 31;
     Params P = P0;
@@ -1752,15 +1752,17 @@ __global__ void __launch_bounds__((TILE || S > 4 || PTS) ? 512 : 256, (TILE || S
         P.sanitize = 1;
     }
     const int warp = threadIdx.x >> 5;
+    // the row-cache area (which also holds the column reduction's TMA ring)
+    // exists for the wide streamed rows only
     WarpShared w = carve(smem_raw + (size_t)warp * P.warp_bytes, TILE ? P.tile_floats : 0, 32 * S,
-                         !TILE);
+                         !TILE && S >= 7);
     const int64_t per = (int64_t)P.N * P.M;
     const uint32_t tile_bytes = (uint32_t)(per * 4);
     uint32_t phase = 0;
     if constexpr (TILE) {
         if (lane == 0) bar_init(w.bar);
         __syncwarp();
-    } else if constexpr (!PTS && FULL) {
+    } else if constexpr (!PTS && FULL && S >= 7) {
         if (lane == 0)
             for (int r = 0; r < kSlots; ++r) bar_init(w.rbar + r);
         __syncwarp();
@@ -1954,24 +1956,26 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     const int KP = 32 * S;
     int tile_floats = 0;
     if (TILE) tile_floats = (int)(((int64_t)P.N * P.M + 31) / 32 * 32);
-    int warp_bytes = tile_floats * 4 + book_bytes(KP, !TILE);
+    int warp_bytes = tile_floats * 4 + book_bytes(KP, !TILE && S >= 7);
     warp_bytes = (warp_bytes + 127) & ~127;
     P.warp_bytes = warp_bytes;
     P.tile_floats = tile_floats;
     int wpb = kSmemLimit / warp_bytes;
-    const int wcap = (TILE || S > 4 || PTS) ? kMaxWarpsPerBlock : 8;
+    const int wcap = (TILE || S > 4 || PTS) ? kMaxWarpsPerBlock : 12;
     if (wpb > wcap) wpb = wcap;
     if (wpb < 1) return TM_ERR_TOO_LARGE;
     const int64_t need_warps = P.B;
     if ((int64_t)wpb > need_warps) wpb = (int)need_warps;
     if (PTS && !TILE && (int64_t)wpb > P.slab_warps) wpb = (int)P.slab_warps;  // one slab per warp
     if (wpb < 1) return TM_ERR_ARG;
-    const int smem = wpb * warp_bytes;
     auto kern = jv_batch_kernel<S, VEC, TILE, FULL, PTS>;
-    // The shared-memory opt-in and the occupancy query run once per device
+    // The shared-memory opt-in and the occupancy queries run once per device
     // and launch shape, so a steady-state launch is just the kernel (nothing
-    // that a CUDA graph capture would reject).
-    struct Cached { int smem = -1, threads = -1, per_sm = 0; };
+    // that a CUDA graph capture would reject).  Streamed dense shapes pick
+    // the block size that keeps the most warps resident: with 96 registers a
+    // thread, 16 warps fill one 512-thread block while two blocks of 10 warps
+    // fit (20 warps).
+    struct Cached { int smem = -1, wpb_max = -1, wpb = 0, per_sm = 0; };
     static Cached cache[64];
     static std::mutex mu;
     int dev = 0;
@@ -1981,17 +1985,32 @@ static int launch_t(const Params &P0, cudaStream_t stream) {
     {
         std::lock_guard<std::mutex> lock(mu);
         Cached &c = cache[dev];
-        if (c.smem != smem || c.threads != wpb * 32) {
+        const int smem_max = wpb * warp_bytes;
+        if (c.smem != smem_max || c.wpb_max != wpb) {
             cudaError_t e =
-                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+                cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_max);
             if (e != cudaSuccess) return cuda_fail(e);
-            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c.per_sm, kern, wpb * 32, smem);
+            int best = wpb, best_per = 0;
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&best_per, kern, wpb * 32, smem_max);
             if (e != cudaSuccess) return cuda_fail(e);
-            c.smem = smem;
-            c.threads = wpb * 32;
+            if (!TILE && !PTS) {
+                for (int cand = wpb - 1; cand >= (wpb + 1) / 2; --cand) {
+                    int per = 0;
+                    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, cand * 32,
+                                                                      cand * warp_bytes);
+                    if (e != cudaSuccess) return cuda_fail(e);
+                    if (cand * per > best * best_per) { best = cand; best_per = per; }
+                }
+            }
+            c.smem = smem_max;
+            c.wpb_max = wpb;
+            c.wpb = best;
+            c.per_sm = best_per;
         }
+        wpb = c.wpb;
         per_sm = c.per_sm;
     }
+    const int smem = wpb * warp_bytes;
     cudaError_t e;
     if (per_sm < 1) per_sm = 1;
     int64_t blocks = (P.B + wpb - 1) / wpb;
@@ -2098,7 +2117,7 @@ static int64_t points_slabs(int64_t B, int N, int M) {
     const int64_t per = (int64_t)N * M;
     const int64_t tile_bytes = ((per + 31) / 32 * 32) * 4 + book_bytes(32 * S, false);
     if (tile_bytes * tile_min_warps() <= kSmemLimit || B <= 0) return 0;
-    const int warp_bytes = (book_bytes(32 * S, true) + 127) & ~127;
+    const int warp_bytes = (book_bytes(32 * S, S >= 7) + 127) & ~127;
     int wpb = kSmemLimit / warp_bytes;
     // the slab kernels launch like the wide ones: up to 16 warps, one block per SM
     if (wpb > kMaxWarpsPerBlock) wpb = kMaxWarpsPerBlock;
