@@ -29,7 +29,8 @@ solver (oracle/_ref, built from the reference sources) on the host cores.
 
 Every named shape is reported in the same line: `per_config` (one GPU) gives,
 for c1, c3, c4 and c5, the op's problems/s on the whole named batch, its solve
-launch's roofline fraction and the reference CPU solver on this host, and
+launch's roofline fraction and the reference CPU solver on this host (and
+`c5_fused`: the config-5 problems built from point sets inside the kernel), and
 `strong_c5` (every N) gives config 5 as strong scaling -- the fixed
 B = 65536 batch split over the N ranks, max over ranks.
 """
@@ -348,6 +349,41 @@ def per_config_record(cfg: str, dev, lib, args, peak: float) -> dict:
     return rec
 
 
+def fused_c5_record(dev, lib, peak: float) -> dict:
+    """Config-5 problems from point sets through the fused op
+    (jonker_sqeuclidean_batch: the costs are built inside the solve kernel),
+    B=65536, x, y ~ N(0, I16): the op per call and its launch through the C
+    ABI, CUDA events.  Algorithmic bytes are the points and the mapping."""
+    import torch
+
+    b, n, d = 65536, 256, 16
+    g = torch.Generator(device=dev).manual_seed(1)
+    x = torch.randn(b, n, d, device=dev, generator=g)
+    y = torch.randn(b, n, d, device=dev, generator=g)
+    op_ms = _device_ms(lambda: torch.ops.assignment.jonker_sqeuclidean_batch(x, y), 3, 1)
+    nbytes = lib.tm_jv_points_workspace_bytes(b, n, n)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    out = torch.empty(b, n, dtype=torch.long, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def kern():
+        rc = lib.tm_jv_points_solve_f32(x.data_ptr(), y.data_ptr(), b, n, n, d, 0.0, 0, 1,
+                                        out.data_ptr(), ws.data_ptr(), nbytes, stream)
+        assert rc == 0, lib.tm_status_string(rc)
+    k_ms = _device_ms(kern, 3, 1)
+    del x, y, ws, out
+    torch.cuda.empty_cache()
+    alg = b * (2 * n * d * 4 + n * 8)
+    return {"workload": f"config5 problems from points: B={b} N=M={n} D={d}, x,y~N(0,I16)",
+            "value": b / (op_ms / 1e3), "unit": UNIT, "ms_per_step": op_ms,
+            "roofline": {"bound": "hbm", "kernel": "jv_batch_kernel (points, check mode)",
+                         "avg_launch_us": k_ms * 1e3, "alg_bytes_per_launch": alg,
+                         "achieved": alg / (k_ms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": alg / (k_ms / 1e3) / 1e9 / peak,
+                         "traffic": traffic_for("c5_fused")},
+            "cost_tensor_bytes_avoided": b * n * n * 4}
+
+
 def strong_c5_record(dev, world: int, rank: int, args) -> dict:
     """Config 5 as strong scaling: the fixed B=65536 batch split into
     `world` contiguous slices, one per rank (each generated on its GPU),
@@ -595,6 +631,7 @@ def run_ours(args):
     if world == 1 and not args.no_per_config:
         per_config = {c: per_config_record(c, dev, lib, args, peak)
                       for c in ("c1", "c3", "c4", "c5")}
+        per_config["c5_fused"] = fused_c5_record(dev, lib, peak)
     strong = strong_c5_record(dev, world, rank, args) if not args.no_per_config else None
     if rank == 0:
         line = {
