@@ -310,8 +310,7 @@ struct WarpShared {
     // row cache of the augmenting row reduction (streaming mode only)
     float2 *centry;    // [row][kCache]: {cost value, column as int bits}
     float *cbound;     // [row]: lower bound of every uncached reduced cost
-    uint8_t *cflag;    // [row]: cache built
-    float *vsh;        // mirror of the prices v
+    float *vsh;        // mirror of the prices v (cached mode: the event buffer)
     // streamed rows: the column reduction's ring of kSlots slots of kChunk
     // rows, filled by TMA bulk copies (it shares the row-cache area, unused
     // until the augmenting row reduction), one mbarrier per slot, the parity
@@ -329,11 +328,17 @@ constexpr int kChunk = 4;  // rows per slot (one bulk copy)
 
 __host__ __device__ inline int slots_for(int K) { return (K + 31) / 32; }
 
-// Per-warp shared bytes: bookkeeping arrays for KP = 32 * S entries.
+// Per-warp shared bytes: bookkeeping arrays for KP = 32 * S entries.  With
+// the row cache (wide streamed rows), arrays whose phases never overlap share
+// space, so 16 warps of K = 256 fit one SM: the price mirror of the row
+// reduction lives in the event buffer of the Dijkstra phase, and the per-row
+// / per-column flags (claim phase, Dijkstra phase) in the cache bounds of the
+// row reduction.
 __host__ __device__ inline int book_bytes(int KP, bool cache) {
     int b = KP * 4 /*dist*/ + KP * 4 /*xrow*/ + KP * 2 * 4 /*ycol,pred,queue,order*/ +
-            KP /*flag*/ + KP * 4 /*evbuf*/ + 48 /*bar + alignment*/;
-    if (cache) b += KP * kCache * 8 + KP * 4 + KP * 4 + KP + 16 + 8 * kSlots + 8;
+            KP * 4 /*evbuf*/ + 48 /*bar + alignment*/;
+    if (cache) b += KP * kCache * 8 /*centry*/ + KP * 4 /*cbound*/ + 8 * kSlots + 8;
+    else b += KP /*flag*/;
     return b;
 }
 
@@ -348,18 +353,17 @@ __device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP,
     w.pred = reinterpret_cast<int16_t *>(p); p += KP * 2;
     w.queue = reinterpret_cast<int16_t *>(p); p += KP * 2;
     w.order = reinterpret_cast<int16_t *>(p); p += KP * 2;
-    w.flag = p; p += KP;
+    if (!cache) { w.flag = p; p += KP; }
     p = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
     w.evbuf = reinterpret_cast<int32_t *>(p); p += KP * 4;
     w.bar = reinterpret_cast<uint64_t *>(p);
     p += 16;
-    w.centry = nullptr; w.cbound = nullptr; w.cflag = nullptr; w.vsh = nullptr;
+    w.centry = nullptr; w.cbound = nullptr; w.vsh = nullptr;
     if (cache) {
         w.centry = reinterpret_cast<float2 *>(p); p += (size_t)KP * kCache * 8;
         w.cbound = reinterpret_cast<float *>(p); p += KP * 4;
-        w.vsh = reinterpret_cast<float *>(p); p += KP * 4;
-        w.cflag = p; p += KP;
-        p = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(p) + 7) & ~uintptr_t(7));
+        w.vsh = reinterpret_cast<float *>(w.evbuf);
+        w.flag = reinterpret_cast<uint8_t *>(w.cbound);
         w.rbar = reinterpret_cast<uint64_t *>(p);
         // kSlots * kChunk rows of KP floats: exactly the row-cache entries' bytes
         static_assert(kSlots * kChunk * 4 == kCache * 8, "the ring must fit the row-cache area");
@@ -1456,8 +1460,13 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
     // finds the prices there)
     if constexpr (use_cache) {
 #pragma unroll
-        for (int s = 0; s < S; ++s)
+        for (int s = 0; s < S; ++s) {
             if (valid >> s & 1) v[s] = w.vsh[jj[s]];
+            // the flags share the cache bounds' space: clear them again for
+            // the Dijkstra phase's event bits
+            const int r = s * 32 + lane;
+            if (r < K) w.flag[r] = 0;
+        }
     } else {
 #pragma unroll
         for (int s = 0; s < S; ++s)
