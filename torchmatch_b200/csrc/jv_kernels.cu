@@ -41,6 +41,9 @@
 #include "torchmatch_b200.h"
 
 namespace tmjv {
+// blocks per SM of the statistics scan (several waves of 8 resident blocks
+// measured faster than one: 5.3 against 4.6 TB/s on 1 GiB)
+constexpr int TMJV_STATS_BPS = 32;
 
 constexpr float kBig = 1e18f;  // LARGE_V<float>, jonker_dense_flat.h:22-23
 constexpr unsigned kFull = 0xffffffffu;
@@ -1866,7 +1869,19 @@ __global__ void __launch_bounds__(256) jv_stats_kernel(const float *__restrict__
     if (vec) {
         const int64_t n4 = n / 4;
         const float4 *x4 = reinterpret_cast<const float4 *>(x);
-        for (int64_t k = tid; k < n4; k += nth) {
+        // four independent 16-byte loads in flight per thread
+        int64_t k = tid;
+        for (; k + 3 * nth < n4; k += 4 * nth) {
+            float4 t[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) t[u] = __ldg(x4 + k + u * nth);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                classify(t[u].x, fl, mk); classify(t[u].y, fl, mk);
+                classify(t[u].z, fl, mk); classify(t[u].w, fl, mk);
+            }
+        }
+        for (; k < n4; k += nth) {
             const float4 t = __ldg(x4 + k);
             classify(t.x, fl, mk); classify(t.y, fl, mk);
             classify(t.z, fl, mk); classify(t.w, fl, mk);
@@ -2180,7 +2195,7 @@ int tm_jv_stats_f32(const float *costs, int64_t count, tm_jv_stats *stats_dev,
     if (count == 0) return TM_OK;
     const int threads = 256;
     int64_t blocks = (count / 4 + threads - 1) / threads;
-    const int64_t cap = (int64_t)tmjv::num_sms() * 8;
+    const int64_t cap = (int64_t)tmjv::num_sms() * TMJV_STATS_BPS;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     tmjv::jv_stats_kernel<<<(unsigned)blocks, threads, 0, stream>>>(costs, count, stats_dev);
