@@ -43,7 +43,7 @@
 namespace tmjv {
 // blocks per SM of the statistics scan (several waves of 8 resident blocks
 // measured faster than one: 5.3 against 4.6 TB/s on 1 GiB)
-constexpr int TMJV_STATS_BPS = 32;
+constexpr int kStatsBlocksPerSm = 32;
 
 constexpr float kBig = 1e18f;  // LARGE_V<float>, jonker_dense_flat.h:22-23
 constexpr unsigned kFull = 0xffffffffu;
@@ -2195,7 +2195,7 @@ int tm_jv_stats_f32(const float *costs, int64_t count, tm_jv_stats *stats_dev,
     if (count == 0) return TM_OK;
     const int threads = 256;
     int64_t blocks = (count / 4 + threads - 1) / threads;
-    const int64_t cap = (int64_t)tmjv::num_sms() * TMJV_STATS_BPS;
+    const int64_t cap = (int64_t)tmjv::num_sms() * tmjv::kStatsBlocksPerSm;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     tmjv::jv_stats_kernel<<<(unsigned)blocks, threads, 0, stream>>>(costs, count, stats_dev);
