@@ -167,6 +167,11 @@ __device__ __forceinline__ int lds_s16_if(bool pred, const int16_t *p, int old) 
         : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"((int)pred), "r"(old));
     return r;
 }
+__device__ __forceinline__ int lds_u8(const uint8_t *p) {
+    int r;
+    asm volatile("ld.shared.u8 %0, [%1];" : "=r"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)));
+    return r;
+}
 __device__ __forceinline__ float lds_f32(const float *p) {
     float r;
     asm volatile("ld.shared.f32 %0, [%1];" : "=f"(r) : "r"((uint32_t)__cvta_generic_to_shared(p)));
@@ -311,7 +316,8 @@ struct WarpShared {
     int32_t *evbuf;    // compacted events of one minimum search
     uint64_t *bar;     // mbarrier of the tile copy
     // row cache of the augmenting row reduction (streaming mode only)
-    float2 *centry;    // [row][kCache]: {cost value, column as int bits}
+    float *cval;       // [row][kCache]: cost value of each cached column
+    uint8_t *ccol;     // [row][kCache]: the cached columns (K <= 256)
     float *cbound;     // [row]: lower bound of every uncached reduced cost
     float *vsh;        // mirror of the prices v (cached mode: the event buffer)
     // streamed rows: the column reduction's ring of kSlots slots of kChunk
@@ -325,9 +331,9 @@ struct WarpShared {
     bool rdead;
 };
 
-constexpr int kCache = 4;  // cached columns per row
-constexpr int kSlots = 2;  // slots of the column reduction's TMA ring
-constexpr int kChunk = 4;  // rows per slot (one bulk copy)
+constexpr int kCache = 6;  // cached columns per row
+constexpr int kSlots = 3;  // slots of the column reduction's TMA ring
+constexpr int kChunk = 2;  // rows per slot (one bulk copy)
 
 __host__ __device__ inline int slots_for(int K) { return (K + 31) / 32; }
 
@@ -340,7 +346,7 @@ __host__ __device__ inline int slots_for(int K) { return (K + 31) / 32; }
 __host__ __device__ inline int book_bytes(int KP, bool cache) {
     int b = KP * 4 /*dist*/ + KP * 4 /*xrow*/ + KP * 2 * 4 /*ycol,pred,queue,order*/ +
             KP * 4 /*evbuf*/ + 48 /*bar + alignment*/;
-    if (cache) b += KP * kCache * 8 /*centry*/ + KP * 4 /*cbound*/ + 8 * kSlots + 8;
+    if (cache) b += KP * kCache * 5 /*cval, ccol*/ + KP * 4 /*cbound*/ + 8 * kSlots + 8;
     else b += KP /*flag*/;
     return b;
 }
@@ -361,16 +367,17 @@ __device__ inline WarpShared carve(unsigned char *base, int tile_floats, int KP,
     w.evbuf = reinterpret_cast<int32_t *>(p); p += KP * 4;
     w.bar = reinterpret_cast<uint64_t *>(p);
     p += 16;
-    w.centry = nullptr; w.cbound = nullptr; w.vsh = nullptr;
+    w.cval = nullptr; w.ccol = nullptr; w.cbound = nullptr; w.vsh = nullptr;
     if (cache) {
-        w.centry = reinterpret_cast<float2 *>(p); p += (size_t)KP * kCache * 8;
+        w.cval = reinterpret_cast<float *>(p); p += (size_t)KP * kCache * 4;
+        w.ccol = p; p += (size_t)KP * kCache;
         w.cbound = reinterpret_cast<float *>(p); p += KP * 4;
         w.vsh = reinterpret_cast<float *>(w.evbuf);
         w.flag = reinterpret_cast<uint8_t *>(w.cbound);
         w.rbar = reinterpret_cast<uint64_t *>(p);
-        // kSlots * kChunk rows of KP floats: exactly the row-cache entries' bytes
-        static_assert(kSlots * kChunk * 4 == kCache * 8, "the ring must fit the row-cache area");
-        w.ring = reinterpret_cast<float *>(w.centry);
+        // kSlots * kChunk rows of KP floats fit in the row-cache entries
+        static_assert(kSlots * kChunk * 4 <= kCache * 5, "the ring must fit the row-cache area");
+        w.ring = w.cval;
     } else {
         w.ring = nullptr;
         w.rbar = nullptr;
@@ -1166,8 +1173,10 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 // column 0 keeps the (then unused) candidate loads in bounds
                 w.cbound[r] = -__int_as_float(0x7f800000);
 #pragma unroll
-                for (int k = 0; k < kCache; ++k)
-                    w.centry[r * kCache + k] = make_float2(0.0f, __int_as_float(0));
+                for (int k = 0; k < kCache; ++k) {
+                    w.cval[r * kCache + k] = 0.0f;
+                    w.ccol[r * kCache + k] = 0;
+                }
             }
             if (valid >> s & 1) w.vsh[jj[s]] = v[s];
         }
@@ -1202,12 +1211,13 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     const unsigned h1 = head + 1, vis1 = visits + 1;
                     const int queued = qnext;
                     // every lane loads a candidate (lanes >= kCache repeat
-                    // one); only lanes < kCache offer theirs
-                    const float2 e = lds_f32x2(w.centry + row * kCache + (lane & (kCache - 1)));
+                    // the first); only lanes < kCache offer theirs
+                    const int ce = row * kCache + (lane < kCache ? lane : 0);
+                    const float ex = lds_f32(w.cval + ce);
+                    const int cj = lds_u8(w.ccol + ce);
                     const float cb = lds_f32(w.cbound + row);
-                    const int cj = __float_as_int(e.y);
                     const float vc = lds_f32(w.vsh + cj);
-                    const float cv = lane < kCache ? e.x - vc : inf;
+                    const float cv = lane < kCache ? ex - vc : inf;
                     const float v1 = warp_min_f(cv);
                     const int j1 = (int)warp_min_u_ord(cv == v1 ? (unsigned)cj : 0xffffffffu);
                     const int i0 = lds_s16(w.ycol + j1);
@@ -1250,9 +1260,8 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                 float cv = __int_as_float(0x7f800000);
                 int cj = 0x7fffffff;
                 if (lane < kCache) {
-                    const float2 e = w.centry[row * kCache + lane];
-                    cj = __float_as_int(e.y);
-                    cv = e.x - w.vsh[cj];
+                    cj = w.ccol[row * kCache + lane];
+                    cv = w.cval[row * kCache + lane] - w.vsh[cj];
                 }
                 v1 = warp_min_f(cv);
                 const bool at1 = cv == v1;
@@ -1309,8 +1318,10 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                         const float m = warp_min_f(a);
                         const int jm = (int)warp_min_u(any && a == m ? (unsigned)ja : 0xffffffffu);
                         const bool won = ja == jm;
-                        if (k < kCache && won)
-                            w.centry[row * kCache + k] = make_float2(sel(c, sa), __int_as_float(jm));
+                        if (k < kCache && won) {
+                            w.cval[row * kCache + k] = sel(c, sa);
+                            w.ccol[row * kCache + k] = (uint8_t)jm;
+                        }
 #pragma unroll
                         for (int t = 0; t < S; ++t)
                             x[t] = (won && t == sa) ? __int_as_float(0x7f800000) : x[t];
