@@ -5,9 +5,11 @@
 // row of the cost matrix is one (or S / VEC vectorised) conflict-free load
 // per lane and every reduction over a row is a single warp reduction
 // (redux.sync on fp32, new with sm_100a).  Column prices v and Dijkstra
-// distances d live in registers of the owning lane; the row-indexed arrays
-// (x, free-row queue) and the column permutation of the Dijkstra phase live
-// in a small per-warp shared-memory block.
+// distances d live in registers of the owning lane (the prices are mirrored
+// in shared memory during the augmenting row reduction); the row of each
+// column (y), the row-indexed arrays (x, free-row queue) and the column
+// permutation of the Dijkstra phase live in a small per-warp shared-memory
+// block.
 //
 // Two storage modes for the cost matrix:
 //   TILE = true   the (N, M) block of the problem is staged into shared
@@ -15,7 +17,12 @@
 //                 and rows are read from there; the next problem is
 //                 prefetched into L2 while the current one is solved.
 //   TILE = false  for matrices that do not fit next to enough warps, rows
-//                 are streamed from L2/HBM with read-only vector loads.
+//                 are streamed from L2/HBM: each claimed problem is
+//                 prefetched into L2, wide square rows (K > 192) pass the
+//                 column reduction through a TMA ring in shared memory, and
+//                 the single rows of the later phases are read with
+//                 read-only vector loads (the wide rows' row reduction keeps
+//                 a per-row cache of its best columns).
 // With PTS (fused cost construction) the kernel builds each problem's
 // squared-Euclidean costs from two point sets itself -- into the tile, or
 // into a per-warp slab of the workspace that then stands in for the input.
