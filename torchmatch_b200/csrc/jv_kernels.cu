@@ -1660,11 +1660,20 @@ __device__ void solve_problem(const float *__restrict__ src, const Params &P, Wa
                     const float rr = c[s] - v[s] - h;
                     const bool upd = (todo >> s & 1) && rr < d[s];
                     d[s] = upd ? rr : d[s];
-                    if (upd) {
-                        w.dist[jj[s]] = rr;
-                        w.pred[jj[s]] = (int16_t)i;
+                    if constexpr (!(FULL && VEC == 4)) {
+                        if (upd) w.dist[jj[s]] = rr;
                     }
+                    if (upd) w.pred[jj[s]] = (int16_t)i;
                     ev |= (upd && rr == dj) ? 1u << s : 0u;
+                }
+                if constexpr (FULL && VEC == 4) {
+                    // a lane's four consecutive columns per group: one
+                    // conflict-free 16-byte store of the mirror (unchanged
+                    // entries are stored as they are)
+#pragma unroll
+                    for (int g = 0; g < S / 4; ++g)
+                        *reinterpret_cast<float4 *>(w.dist + jj[4 * g]) =
+                            make_float4(d[4 * g], d[4 * g + 1], d[4 * g + 2], d[4 * g + 3]);
                 }
                 if (!__any_sync(kFull, ev != 0)) continue;
                 // tie events: order them by position
